@@ -1,0 +1,135 @@
+// C ABI entry points: argument validation, dispatch, thread-local error text.
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace hb {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return HYENA_OK;
+  return fail(HYENA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int fir_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A, cudaStream_t st);
+int hcl_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A, void* ws,
+                       size_t ws_bytes, cudaStream_t st);
+size_t hcl_workspace_size(int H, int T, int nseg);
+int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaStream_t st);
+int quant_e4m3_launch(const void* x, int64_t ldx, void* q, int64_t ldq, int M, int K,
+                      const float* scale, cudaStream_t st);
+int gemm_e4m3_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                     int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
+                     cudaStream_t st);
+int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                     int64_t ldo, int M, int N, int K, const void* bias, cudaStream_t st);
+
+static int check_params(const hyena_layer_params* p) {
+  HB_REQUIRE(p != nullptr, "null layer params");
+  HB_REQUIRE(p->H > 0 && p->H % 64 == 0, "H must be a positive multiple of 64");
+  HB_REQUIRE(p->short_w != nullptr, "short_w is null");
+  if (p->kind == HYENA_KIND_FIR) {
+    HB_REQUIRE(p->inner_w != nullptr, "FIR inner_w is null");
+    HB_REQUIRE(p->K == 7 || p->K == 128, "FIR K must be 7 or 128");
+  } else if (p->kind == HYENA_KIND_IIR) {
+    HB_REQUIRE(p->log_poles != nullptr && p->residues != nullptr, "IIR poles/residues are null");
+    HB_REQUIRE(p->K == 16, "IIR modal order must be 16");
+  } else {
+    return fail(HYENA_ERR_INVALID, "unknown mixer kind");
+  }
+  return HYENA_OK;
+}
+
+static int check_view(const hyena_state_view& v, const char* name, int min_cols) {
+  if (v.data == nullptr) return fail(HYENA_ERR_INVALID, std::string(name) + ": null data");
+  if (v.cols < min_cols)
+    return fail(HYENA_ERR_INVALID, std::string(name) + ": too few window columns");
+  if (v.num_blocks <= 0) return fail(HYENA_ERR_INVALID, std::string(name) + ": no blocks");
+  return HYENA_OK;
+}
+
+}  // namespace hb
+
+using namespace hb;
+
+extern "C" {
+
+int hyena_abi_version(void) { return HYENA_ABI_VERSION; }
+
+const char* hyena_last_error(void) { return g_last_error.c_str(); }
+
+size_t hyena_prefill_workspace_size(const hyena_layer_params* p, int32_t T, int32_t nseg) {
+  if (p == nullptr || p->kind != HYENA_KIND_IIR) return 0;
+  return hcl_workspace_size(p->H, T < 0 ? 0 : T, nseg < 0 ? 0 : nseg);
+}
+
+int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_args* a, void* ws,
+                  size_t ws_bytes, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  HB_REQUIRE(a != nullptr, "null prefill args");
+  HB_REQUIRE(a->T >= 0 && a->num_segments >= 0, "negative sizes");
+  if (a->T == 0 || a->num_segments == 0) return HYENA_OK;
+  HB_REQUIRE(a->z && a->out && a->query_start_loc && a->state_indices, "null prefill pointer");
+  HB_REQUIRE(aligned16(a->z) && a->ldz % 8 == 0, "z must be 16-byte aligned with ldz % 8 == 0");
+  HB_REQUIRE(a->ldz >= 3LL * p->H && a->ldo >= p->H, "row strides too small");
+  if ((rc = check_view(a->conv_state, "conv_state", 2))) return rc;
+  if (p->kind == HYENA_KIND_FIR) {
+    if ((rc = check_view(a->inner_state, "inner_state", p->K - 1))) return rc;
+  } else {
+    if ((rc = check_view(a->inner_state, "inner_state", 16))) return rc;
+  }
+  HB_REQUIRE(a->conv_state.cols <= 8, "conv window wider than 8 columns");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->kind == HYENA_KIND_FIR) return fir_prefill_launch(*p, *a, st);
+  return hcl_prefill_launch(*p, *a, ws, ws_bytes, st);
+}
+
+int hyena_decode(const hyena_layer_params* p, const hyena_decode_args* a, void* stream) {
+  int rc = check_params(p);
+  if (rc) return rc;
+  HB_REQUIRE(a != nullptr, "null decode args");
+  if (a->num_reqs <= 0) return HYENA_OK;
+  HB_REQUIRE(a->z && a->out && a->conv_in_block && a->conv_out_block && a->in_slots &&
+                 a->out_slots,
+             "null decode pointer");
+  HB_REQUIRE(a->q >= 1 && a->q <= 8, "q must be in [1, 8]");
+  HB_REQUIRE(a->ldz >= 3LL * p->H && a->ldo >= p->H, "row strides too small");
+  if ((rc = check_view(a->conv_state, "conv_state", 2))) return rc;
+  if ((rc = check_view(a->inner_state, "inner_state", p->kind == HYENA_KIND_FIR ? p->K - 1 : 16)))
+    return rc;
+  return decode_launch(*p, *a, static_cast<cudaStream_t>(stream));
+}
+
+int hyena_quant_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, int32_t M, int32_t K,
+                     const float* input_scale, void* stream) {
+  HB_REQUIRE(x && q && input_scale, "null quant pointer");
+  return quant_e4m3_launch(x, ldx, q, ldq, M, K, input_scale, static_cast<cudaStream_t>(stream));
+}
+
+int hyena_gemm_e4m3(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                    int64_t ldo, int32_t M, int32_t N, int32_t K, const float* scale_a,
+                    const float* scale_b, void* stream) {
+  HB_REQUIRE(A && B && out && scale_a && scale_b, "null gemm pointer");
+  return gemm_e4m3_launch(A, lda, B, ldb, out, ldo, M, N, K, scale_a, scale_b,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                    int64_t ldo, int32_t M, int32_t N, int32_t K, const void* bias,
+                    void* stream) {
+  HB_REQUIRE(A && B && out, "null gemm pointer");
+  return gemm_bf16_launch(A, lda, B, ldb, out, ldo, M, N, K, bias,
+                          static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,348 @@
+// tcgen05 projection GEMMs for the Hyena mixer (sm_100a).
+//
+//   in_proj : out(M,N) bf16 = (A e4m3 . B e4m3^T) * sa * sb     (kind::f8f6f4)
+//   out_proj: out(M,N) bf16 =  A bf16 . B bf16^T + bias          (kind::f16)
+// Both operands K-major (activations (M,K) row-major, nn.Linear weights (N,K)).
+//
+// One CTA computes a 128x256 tile with an fp32 accumulator in tensor memory:
+//   warp 0     TMA producer: 128-byte-wide K slabs of A and B, SWIZZLE_128B,
+//              into a 4-stage shared-memory ring (no multicast)
+//   warp 1     TMEM allocation + single-thread tcgen05.mma issue; each stage is
+//              released by tcgen05.commit onto its "empty" mbarrier
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, scale / bias, bf16,
+//              16-byte global stores
+// Every mbarrier wait is bounded by a globaltimer budget; on expiry the kernel
+// records the event in a device counter and runs to completion (TMEM freed).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace hb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BKB = 128;  // bytes of K per stage (one 128B swizzle row)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB;
+constexpr int B_BYTES = BN * BKB;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr unsigned long long WAIT_BUDGET_NS = 4000000000ull;  // 4 s
+
+struct __align__(1024) Smem {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full;
+  uint32_t tmem_base;
+};
+
+__device__ int g_wait_timeouts;
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  if (mbar_try_wait(b, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (true) {
+    if (mbar_try_wait(b, parity)) return true;
+    if (now_ns() - t0 > WAIT_BUDGET_NS) {
+      atomicAdd(&g_wait_timeouts, 1);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// K-major, SWIZZLE_128B shared-memory matrix descriptor: 8-row core groups
+// 1024 B apart (SBO), LBO unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+  const uint64_t addr = su32(p);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+template <bool FP8>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                    uint32_t accumulate) {
+  if constexpr (FP8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  }
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Instruction descriptor: fp32 accumulator, K-major A and B, M=128, N=256;
+// operand format E4M3 (kind::f8f6f4) or BF16 (kind::f16).
+template <bool FP8>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (1u << 4) | ((FP8 ? 0u : 1u) << 7) | ((FP8 ? 0u : 1u) << 10) |
+         (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
+            const float* __restrict__ sa, const float* __restrict__ sb,
+            const bf16* __restrict__ bias) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  constexpr int ELEM = FP8 ? 1 : 2;
+  constexpr int KE = BKB / ELEM;  // K elements per stage
+  const int kblocks = K / KE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    mbar_init(&S.tmem_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&S.tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(&S.empty[s], ph ^ 1)) break;
+        mbar_expect_tx(&S.full[s], STAGE_BYTES);
+        tma_load_2d(&tmA, &S.full[s], S.a[s], kb * KE, m0);
+        tma_load_2d(&tmB, &S.full[s], S.b[s], kb * KE, n0);
+        issued = kb + 1;
+      }
+      // Drain: every issued copy has landed before the CTA can exit.
+      for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
+        mbar_wait(&S.full[kb % STAGES], (kb / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID = idesc<FP8>();
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(&S.full[s], ph)) break;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKB / 32; ++kk) {
+          const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
+          const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
+          mma<FP8>(tmem, ad, bd, ID, (kb | kk) != 0 ? 1u : 0u);
+        }
+        mma_commit(&S.empty[s]);
+      }
+      mma_commit(&S.tmem_full);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool ok = mbar_wait(&S.tmem_full, 0);
+    fence_after();
+    const int row = m0 + 32 * q + lane;
+    float scale_a = 1.0f, scale_b = 1.0f;
+    if constexpr (FP8) {
+      scale_a = __ldg(sa);
+      scale_b = __ldg(sb);
+    }
+#pragma unroll 1
+    for (int cb = 0; cb < BN / 32; ++cb) {
+      uint32_t r[32];
+      tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r);
+      const int col0 = n0 + cb * 32;
+      if (!ok || row >= M || col0 >= N) continue;
+      bf16* dst = out + (long long)row * ldo + col0;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        if (col0 + 8 * v >= N) break;
+        uint4 pk;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x0 = __uint_as_float(r[8 * v + 2 * e]);
+          float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
+          if constexpr (FP8) {
+            x0 = (x0 * scale_a) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+            x1 = (x1 * scale_a) * scale_b;
+          } else {
+            if (bias != nullptr) {
+              x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
+              x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
+            }
+          }
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+          pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static int make_map(CUtensorMap* m, const void* base, bool fp8, uint64_t inner, uint64_t outer,
+                    uint64_t ld_elems, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(HYENA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const int elem = fp8 ? 1 : 2;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * elem};
+  cuuint32_t box[2] = {uint32_t(BKB / elem), box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HYENA_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return HYENA_OK;
+}
+
+template <bool FP8>
+static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out, int64_t ldo,
+                  int M, int N, int K, const float* sa, const float* sb, const void* bias,
+                  cudaStream_t st) {
+  if (M <= 0 || N <= 0) return HYENA_OK;
+  const int KE = BKB / (FP8 ? 1 : 2);
+  HB_REQUIRE(K > 0 && K % KE == 0, FP8 ? "e4m3 GEMM needs K % 128 == 0" : "bf16 GEMM needs K % 64 == 0");
+  HB_REQUIRE(N % 8 == 0 && ldo % 8 == 0, "GEMM needs N % 8 == 0 and ldo % 8 == 0");
+  HB_REQUIRE(aligned16(A) && aligned16(B) && aligned16(out), "GEMM operands must be 16-byte aligned");
+  HB_REQUIRE((lda * (FP8 ? 1 : 2)) % 16 == 0 && (ldb * (FP8 ? 1 : 2)) % 16 == 0,
+             "GEMM row strides must be multiples of 16 bytes");
+  HB_REQUIRE(lda >= K && ldb >= K && ldo >= N, "GEMM leading dimensions too small");
+  CUtensorMap ta, tb;
+  int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
+  if (rc) return rc;
+  if ((rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN))) return rc;
+  const size_t smem = sizeof(Smem) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(gemm)");
+    attr = true;
+  }
+  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+  gemm_kernel<FP8><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N, K,
+                                                sa, sb, static_cast<const bf16*>(bias));
+  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+}
+
+}  // namespace gemm
+
+int gemm_e4m3_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                     int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
+                     cudaStream_t st) {
+  return gemm::launch<true>(A, lda, B, ldb, out, ldo, M, N, K, sa, sb, nullptr, st);
+}
+
+int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                     int64_t ldo, int M, int N, int K, const void* bias, cudaStream_t st) {
+  return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, st);
+}
+
+}  // namespace hb

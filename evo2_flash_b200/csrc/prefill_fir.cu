@@ -1,0 +1,402 @@
+// Fused Hyena FIR prefill (HCS K=7, HCM K=128) for sm_100a.
+//
+// One launch computes, for every packed prefill row t and channel h,
+//   (x2, x1, v) = K=3 causal FIR over the in_proj triple      (vLLM causal_conv1d_fn)
+//   u           = bf16(x1 * v)                                 (mixers.py:1293)
+//   y           = bf16( sum_k w[h,k] * u[t-K+1+k] )            (triton_prefill.py:391-430)
+//   g           = bf16(x2 * [bf16(y + bf16(D*u))  | y])        (mixers.py:1300-1302)
+// with left context from the cached windows (S0 for the K=3 filter, S1 for the
+// inner filter) when a segment continues a sequence, zeros otherwise.  A second
+// launch writes each segment's final windows (triton_prefill.py:433-459), so no
+// CTA can read a window another CTA already overwrote.
+//
+// Layout: a CTA owns 64 channels (192 z columns) and a contiguous range of packed
+// rows, and slides along time: u values live in a shared-memory ring indexed by
+// row, so the inner FIR's (K-1)-row halo is recomputed only once per CTA range
+// and at segment starts, not per tile.  Every z row is read once from HBM with
+// 16-byte vector loads; g is written once.
+#include "common.cuh"
+
+namespace hb {
+
+constexpr int FIR_CG = 64;       // channels per CTA
+constexpr int FIR_BT = 64;       // rows per tile
+constexpr int FIR_THREADS = 256;
+constexpr int FIR_RPT = 16;      // output rows per thread in the tap loop
+constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
+
+template <int K>
+struct FirCfg {
+  static constexpr int HIST = K - 1;
+  static constexpr int RING = ((HIST + FIR_BT + 15) / 16) * 16;
+};
+
+template <int K>
+struct FirShared {
+  float ring[FirCfg<K>::RING][FIR_CG];  // u by row (mod RING), fp32 (state values are fp32)
+  bf16 zt[FIR_BT][3 * FIR_CG];          // z tile
+  bf16 x2s[FIR_BT][FIR_CG];             // x2 of the tile
+  bf16 wsm[K][FIR_CG];                  // inner taps, [k][c]
+  float zh[2][3 * FIR_CG];              // z rows (r-2, r-1) before the tile
+  float sw[3][3 * FIR_CG];              // short taps [tap][col]
+  float dsm[FIR_CG];
+};
+
+template <int RING>
+__device__ __forceinline__ int ring_idx(long long t) {
+  long long m = t % RING;
+  return int(m < 0 ? m + RING : m);
+}
+
+struct SegCtx {
+  int a, e;       // segment rows
+  long long blk;  // state block (valid only if init)
+  bool init;
+};
+
+__device__ __forceinline__ SegCtx load_segment(const hyena_prefill_args& A, int j) {
+  SegCtx s;
+  s.a = __ldg(A.query_start_loc + j);
+  s.e = __ldg(A.query_start_loc + j + 1);
+  s.blk = __ldg(A.state_indices + (long long)j * A.state_indices_stride);
+  s.init = A.has_initial_state != nullptr && __ldg(A.has_initial_state + j) != 0;
+  return s;
+}
+
+// z value of row t, column col (absolute z column), honouring the segment's
+// left context: rows before the segment come from the cached S0 window.
+__device__ __forceinline__ float z_at(const hyena_prefill_args& A, const SegCtx& s, long long t,
+                                      int col) {
+  const bf16* z = static_cast<const bf16*>(A.z);
+  if (t >= s.a) return ldbf(z + t * A.ldz + col);
+  if (!s.init) return 0.0f;
+  const long long back = s.a - t;  // 1 = newest cached input, in column 1
+  if (back > 2) return 0.0f;
+  const bf16* s0 = static_cast<const bf16*>(A.conv_state.data);
+  return ldbf(s0 + s.blk * A.conv_state.block_stride + (2 - back) * A.conv_state.col_stride +
+              (long long)col * A.conv_state.dim_stride);
+}
+
+// u = bf16(x1 * v) of row t >= s.a for channel h, straight from global memory
+// (used for halos only).
+__device__ __forceinline__ float u_at(const hyena_prefill_args& A, const hyena_layer_params& P,
+                                      const SegCtx& s, long long t, int h) {
+  const bf16* sw = static_cast<const bf16*>(P.short_w);
+  float val[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int col = 3 * h + 1 + q;
+    val[q] = short_tap(z_at(A, s, t - 2, col), z_at(A, s, t - 1, col), z_at(A, s, t, col),
+                       ldbf(sw + col * 3), ldbf(sw + col * 3 + 1), ldbf(sw + col * 3 + 2));
+  }
+  return bf16r(val[0] * val[1]);
+}
+
+template <int K>
+__global__ void __launch_bounds__(FIR_THREADS, 2)
+fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
+  constexpr int RING = FirCfg<K>::RING;
+  constexpr int HIST = K - 1;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  FirShared<K>& S = *reinterpret_cast<FirShared<K>*>(smem_raw);
+
+  const int tid = threadIdx.x;
+  const int c0 = blockIdx.y * FIR_CG;
+  const int nseg = A.num_segments;
+  const int32_t* qsl = A.query_start_loc;
+  const int T_end = min(A.T, __ldg(qsl + nseg));
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(T_end, r0 + rows_per_cta);
+  if (r0 >= r1) return;
+
+  const bf16* z = static_cast<const bf16*>(A.z);
+  bf16* out = static_cast<bf16*>(A.out);
+  const bf16* iw = static_cast<const bf16*>(P.inner_w);
+  const bf16* swg = static_cast<const bf16*>(P.short_w);
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  const float* s1 = static_cast<const float*>(A.inner_state.data);
+
+  for (int i = tid; i < K * FIR_CG; i += FIR_THREADS) {
+    const int k = i / FIR_CG, c = i % FIR_CG;
+    S.wsm[k][c] = iw[(long long)(c0 + c) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k];
+  }
+  for (int i = tid; i < 9 * FIR_CG; i += FIR_THREADS) {
+    const int col = i / 3, tap = i % 3;
+    S.sw[tap][col] = ldbf(swg + (long long)(3 * c0 + col) * 3 + tap);
+  }
+  if (tid < FIR_CG) S.dsm[tid] = Dg ? ldbf(Dg + c0 + tid) : 0.0f;
+  __syncthreads();
+
+  const int c = tid % FIR_CG;  // channel of this thread in the gate / FIR phases
+  const int rl = tid / FIR_CG; // 0..3
+
+  int r = r0;
+  int j = find_segment(qsl, nseg, r);
+  while (r < r1) {
+    while (j < nseg && __ldg(qsl + j + 1) <= r) ++j;
+    if (j >= nseg) break;
+    SegCtx seg = load_segment(A, j);
+    if (seg.a > r) { r = seg.a; continue; }  // defensive: qsl must tile the rows
+    if (seg.init && (seg.blk < 0 || seg.blk >= A.inner_state.num_blocks ||
+                     seg.blk >= A.conv_state.num_blocks)) {
+      if (tid == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+      seg.init = false;
+    }
+
+    // ---- history for row r: ring rows [r-HIST, r) and z rows r-2, r-1
+    for (int i = tid; i < HIST * FIR_CG; i += FIR_THREADS) {
+      const int m = i / FIR_CG + 1, cc = i % FIR_CG;
+      const long long t = (long long)r - m;
+      float val;
+      if (t >= seg.a) {
+        val = u_at(A, P, seg, t, c0 + cc);
+      } else if (seg.init && seg.a - t <= HIST) {
+        const long long col = HIST - (seg.a - t);
+        val = s1[seg.blk * A.inner_state.block_stride + col * A.inner_state.col_stride +
+                 (long long)(c0 + cc) * A.inner_state.dim_stride];
+      } else {
+        val = 0.0f;
+      }
+      S.ring[ring_idx<RING>(t)][cc] = val;
+    }
+    for (int i = tid; i < 2 * 3 * FIR_CG; i += FIR_THREADS) {
+      const int q = i / (3 * FIR_CG), col = i % (3 * FIR_CG);
+      S.zh[q][col] = z_at(A, seg, (long long)r - 2 + q, 3 * c0 + col);
+    }
+    __syncthreads();
+
+    const int end = min(seg.e, r1);
+    while (r < end) {
+      const int n = min(FIR_BT, end - r);
+      // ---- stage z rows [r, r+n) x 192 columns (16-byte vectors)
+      constexpr int VPR = 3 * FIR_CG * 2 / 16;  // vectors per row
+      for (int i = tid; i < n * VPR; i += FIR_THREADS) {
+        const int row = i / VPR, v = i % VPR;
+        const uint4 val = __ldg(reinterpret_cast<const uint4*>(z + (long long)(r + row) * A.ldz +
+                                                               3 * c0) + v);
+        *(reinterpret_cast<uint4*>(&S.zt[row][0]) + v) = val;
+      }
+      __syncthreads();
+
+      // ---- K=3 short filter, de-interleave, u = x1*v
+      for (int row = rl; row < n; row += FIR_THREADS / FIR_CG) {
+        float o[3];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          const int col = 3 * c + q;
+          const float xm2 = row >= 2 ? __bfloat162float(S.zt[row - 2][col]) : S.zh[row][col];
+          const float xm1 = row >= 1 ? __bfloat162float(S.zt[row - 1][col]) : S.zh[1][col];
+          const float x0 = __bfloat162float(S.zt[row][col]);
+          o[q] = short_tap(xm2, xm1, x0, S.sw[0][col], S.sw[1][col], S.sw[2][col]);
+        }
+        S.ring[ring_idx<RING>((long long)r + row)][c] = bf16r(o[1] * o[2]);
+        S.x2s[row][c] = __float2bfloat16_rn(o[0]);
+      }
+      __syncthreads();
+
+      // ---- z history for the next tile (reads zt/zh only; ring untouched)
+      if (tid < 3 * FIR_CG) {
+        const int col = tid;
+        float h0, h1;
+        if (n >= 2) {
+          h0 = __bfloat162float(S.zt[n - 2][col]);
+          h1 = __bfloat162float(S.zt[n - 1][col]);
+        } else {
+          h0 = S.zh[1][col];
+          h1 = __bfloat162float(S.zt[0][col]);
+        }
+        S.zh[0][col] = h0;
+        S.zh[1][col] = h1;
+      }
+
+      // ---- inner FIR over the ring: thread = (channel c, rows i0..i0+15)
+      const int i0 = rl * FIR_RPT;
+      if (i0 < n) {
+        float acc[FIR_RPT];
+#pragma unroll
+        for (int q = 0; q < FIR_RPT; ++q) acc[q] = 0.0f;
+        const int idx0 = ring_idx<RING>((long long)r + i0 - HIST);
+        float cur[16], nxt[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          int id = idx0 + x;
+          id -= id >= RING ? RING : 0;
+          cur[x] = S.ring[id][c];
+        }
+#pragma unroll
+        for (int kb = 0; kb < K; kb += 16) {
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            if (kb + 16 + x < HIST + FIR_RPT) {
+              int id = idx0 + kb + 16 + x;
+              id -= id >= RING ? RING : 0;
+              nxt[x] = S.ring[id][c];
+            }
+          }
+#pragma unroll
+          for (int kk = 0; kk < 16; ++kk) {
+            if (kb + kk < K) {
+              const float w = __bfloat162float(S.wsm[kb + kk][c]);
+#pragma unroll
+              for (int q = 0; q < FIR_RPT; ++q) {
+                const float uv = (q + kk < 16) ? cur[q + kk] : nxt[q + kk - 16];
+                acc[q] = fmaf(w, uv, acc[q]);
+              }
+            }
+          }
+#pragma unroll
+          for (int x = 0; x < 16; ++x) cur[x] = nxt[x];
+        }
+        const float d = S.dsm[c];
+        const bool has_d = Dg != nullptr;
+#pragma unroll
+        for (int q = 0; q < FIR_RPT; ++q) {
+          if (i0 + q < n) {
+            float y = bf16r(acc[q]);
+            if (has_d) {
+              int id = idx0 + q + HIST;
+              id -= id >= RING ? RING : 0;
+              const float u = S.ring[id][c];
+              y = bf16r(y + bf16r(d * u));
+            }
+            const float g = bf16r(__bfloat162float(S.x2s[i0 + q][c]) * y);
+            out[(long long)(r + i0 + q) * A.ldo + c0 + c] = __float2bfloat16_rn(g);
+          }
+        }
+      }
+      __syncthreads();
+      r += n;
+    }
+    ++j;
+  }
+}
+
+// Second launch: each segment's final windows.  S0 columns 0..1 <- last two z
+// values of concat(old S0[:, 0:2] | zeros, z_seg) (mixers.py:374, 380-382; any
+// speculative columns 2..W0-1 are left as they are); S1[:, :K-1] <- last K-1 u
+// values of concat(old S1 | zeros, u_seg) (triton_prefill.py:433-459).
+// K == 0 updates S0 only.
+template <int K>
+__global__ void __launch_bounds__(128)
+prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
+  const int j = blockIdx.x;
+  const int h = blockIdx.y * 128 + threadIdx.x;
+  if (h >= P.H) return;
+  SegCtx seg = load_segment(A, j);
+  const int L = seg.e - seg.a;
+  if (L <= 0) return;
+  if (seg.blk < 0 || seg.blk >= A.conv_state.num_blocks ||
+      (K > 0 && seg.blk >= A.inner_state.num_blocks)) {
+    if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+    return;
+  }
+  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const bf16* z = static_cast<const bf16*>(A.z);
+
+  // Old S0 columns 0..1 for the three z columns of channel h (read before any write).
+  float old0[3][2];
+#pragma unroll
+  for (int q = 0; q < 3; ++q)
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      old0[q][i] = seg.init ? ldbf(s0 + seg.blk * A.conv_state.block_stride +
+                                   (long long)i * A.conv_state.col_stride +
+                                   (long long)(3 * h + q) * A.conv_state.dim_stride)
+                            : 0.0f;
+
+  if constexpr (K > 0) {
+    constexpr int HIST = K - 1;
+    float* s1 = static_cast<float*>(A.inner_state.data);
+    const bf16* sw = static_cast<const bf16*>(P.short_w);
+    float w1[3], w2[3];
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      w1[q] = ldbf(sw + (3 * h + 1) * 3 + q);
+      w2[q] = ldbf(sw + (3 * h + 2) * 3 + q);
+    }
+    float* base = s1 + seg.blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride;
+    for (int i = 0; i < HIST; ++i) {
+      const int src = L + i;  // position in concat(hist[HIST], u[L])
+      float val;
+      if (src < HIST) {
+        val = seg.init ? base[(long long)src * A.inner_state.col_stride] : 0.0f;
+      } else {
+        const long long t = (long long)seg.a + (src - HIST);
+        float xv[2][3];
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+          const long long tt = t - 2 + m;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            float v;
+            if (tt >= seg.a) {
+              v = ldbf(z + tt * A.ldz + 3 * h + 1 + q);
+            } else {
+              const int back = int(seg.a - tt);  // 1..2
+              v = back == 1 ? old0[1 + q][1] : old0[1 + q][0];
+            }
+            xv[q][m] = v;
+          }
+        }
+        const float x1 = short_tap(xv[0][0], xv[0][1], xv[0][2], w1[0], w1[1], w1[2]);
+        const float vv = short_tap(xv[1][0], xv[1][1], xv[1][2], w2[0], w2[1], w2[2]);
+        val = bf16r(x1 * vv);
+      }
+      base[(long long)i * A.inner_state.col_stride] = val;
+    }
+  }
+
+  // New S0 columns 0..1.
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int src = L + i;  // position in concat(old[0:2], z[L])
+      const float val = src < 2 ? old0[q][src]
+                                : ldbf(z + (long long)(seg.a + src - 2) * A.ldz + 3 * h + q);
+      s0[seg.blk * A.conv_state.block_stride + (long long)i * A.conv_state.col_stride +
+         (long long)(3 * h + q) * A.conv_state.dim_stride] = __float2bfloat16_rn(val);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+template <int K>
+static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, cudaStream_t st) {
+  const size_t smem = sizeof(FirShared<K>);
+  static bool attr_set = false;  // per process; the attribute is per function
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(fir_prefill_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(fir_prefill)");
+    attr_set = true;
+  }
+  // Rows per CTA: long enough that the (K-1)-row halo is a small fraction,
+  // short enough to fill the 148 SMs.
+  const int groups = P.H / FIR_CG;
+  int rows = K > 16 ? 1024 : 256;
+  const long long want_ctas = 148LL * 2 * 3;  // ~3 waves of 2 CTAs per SM
+  while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
+  dim3 grid((A.T + rows - 1) / rows, groups);
+  fir_prefill_kernel<K><<<grid, FIR_THREADS, smem, st>>>(P, A, rows);
+  int rc = check_launch("fir_prefill_kernel");
+  if (rc) return rc;
+  dim3 g2(A.num_segments, (P.H + 127) / 128);
+  prefill_state_kernel<K><<<g2, 128, 0, st>>>(P, A);
+  return check_launch("prefill_state_kernel");
+}
+
+int fir_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A, cudaStream_t st) {
+  if (P.K == 128) return launch_fir<128>(P, A, st);
+  if (P.K == 7) return launch_fir<7>(P, A, st);
+  return fail(HYENA_ERR_UNSUPPORTED, "FIR prefill supports K = 7 or 128");
+}
+
+int conv_state_update_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
+                             cudaStream_t st) {
+  dim3 g2(A.num_segments, (P.H + 127) / 128);
+  prefill_state_kernel<0><<<g2, 128, 0, st>>>(P, A);
+  return check_launch("prefill_state_kernel<0>");
+}
+
+}  // namespace hb

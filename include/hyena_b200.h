@@ -1,0 +1,185 @@
+/*
+ * hyena_b200.h -- C ABI of the B200 (sm_100a) Hyena-mixer kernels.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * launches asynchronously on the caller's CUDA stream, performs no host<->device
+ * synchronisation and never allocates device memory (workspace, where needed, is
+ * caller-provided and sized by the matching *_workspace_size function).
+ * All functions return HYENA_OK (0) or an error code; hyena_last_error() gives a
+ * human-readable message for the calling thread.  Device-side range violations
+ * (a state block index outside [0, num_blocks)) never trap: the offending row is
+ * skipped and a bit is OR-ed into the optional caller-provided `error_flags` word.
+ *
+ * Paged mixer state follows the layout vLLM hands the reference mixers
+ * (evo2_flash/mixers.py:6-17, 892-904, 940-949):
+ *   S0  conv window over the 3H in_proj channels, bf16, (blocks, W0, 3H) in vLLM's
+ *       SD layout (W0 = K_short-1 [+ num_spec]); oldest column first.
+ *   S1  inner-FIR window over H channels, fp32, (blocks, 127, H); HCS uses the
+ *       first 6 columns, HCM all 127.
+ *   S2  LI modal state, fp32, (blocks, H, 16[+1 stamp column]).
+ * Each slice is described by a hyena_state_view with explicit strides, so the
+ * dim-first and the SD orientation, and vLLM's padded page strides, all work.
+ */
+#ifndef HYENA_B200_H
+#define HYENA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HYENA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define HYENA_API __attribute__((visibility("default")))
+#else
+#define HYENA_API
+#endif
+
+#define HYENA_OK 0
+#define HYENA_ERR_INVALID 1      /* bad argument (shape, alignment, null pointer) */
+#define HYENA_ERR_CUDA 2         /* a CUDA runtime/driver call failed */
+#define HYENA_ERR_UNSUPPORTED 3  /* a configuration the kernels do not implement */
+
+/* Bits OR-ed into *error_flags by the kernels. */
+#define HYENA_FLAG_BLOCK_RANGE 1 /* a state block index was outside [0, num_blocks) */
+#define HYENA_FLAG_SEGMENT 2     /* query_start_loc was not non-decreasing / exceeded T */
+
+typedef struct hyena_state_view {
+  void* data;            /* element (block 0, column 0, channel 0) */
+  int64_t block_stride;  /* elements between consecutive blocks (vLLM page stride) */
+  int64_t col_stride;    /* elements between window columns (time positions) */
+  int64_t dim_stride;    /* elements between channels */
+  int32_t cols;          /* window columns available in the slice */
+  int32_t num_blocks;    /* valid block indices are [0, num_blocks) */
+} hyena_state_view;
+
+/* Mixer kinds. */
+#define HYENA_KIND_FIR 0  /* HCS (K=7) and HCM (K=128) explicit depthwise FIR */
+#define HYENA_KIND_IIR 1  /* HCL diagonal modal SSM of order 16 */
+
+/* Parameters shared by prefill and decode of one Hyena layer.  Channel h of the
+ * in_proj output occupies columns (3h, 3h+1, 3h+2) = (x2, x1, v) of z. */
+typedef struct hyena_layer_params {
+  int32_t kind;          /* HYENA_KIND_FIR / HYENA_KIND_IIR */
+  int32_t H;             /* channels of this shard (multiple of 64) */
+  int32_t K;             /* FIR taps (7 or 128); 16 (modal order) for IIR */
+  const void* short_w;   /* (3H, 3) bf16 contiguous, cross-correlation order */
+  const void* inner_w;   /* FIR: (H, K) bf16 taps, w[:, K-1] pairs with the current sample */
+  int64_t inner_w_stride_h, inner_w_stride_k;
+  const float* log_poles;/* IIR: (H, 16) fp32 */
+  int64_t lp_stride_h, lp_stride_s;
+  const float* residues; /* IIR: (H, 16) fp32 */
+  int64_t res_stride_h, res_stride_s;
+  const void* D;         /* (H,) bf16 skip, or NULL (HCS has none) */
+} hyena_layer_params;
+
+/* ---------------------------------------------------------------- prefill
+ * Replaces, for the prefill rows of one step:
+ *   HyenaMixerBase._short_conv prefill branch -> vLLM causal_conv1d_fn
+ *     (evo2_flash/mixers.py:1121-1151, torch twin 350-383), the de-interleave and
+ *     x1*v gate (mixers.py:1207-1208, 1293, 1356);
+ *   FIR: HyenaFIRMixer._inner_prefill -> triton_prefill.fir_prefill
+ *     (mixers.py:1258-1262; triton_prefill.py:391-501) and the +D*u, *x2 gate
+ *     (mixers.py:1300-1302);
+ *   IIR: the per-segment loop of HyenaIIRMixer._forward_impl and iir_segment,
+ *     hcl_compute_filter, iir_final_state (mixers.py:144-210, 1378-1397;
+ *     triton_hcl.py:88-123; triton_prefill.py:351-387).
+ * Input z: (T, 3H) bf16 packed prefill rows (row 0 = first prefill token).
+ * Output g: (T, H) bf16 = x2 * (inner(u) [+ D*u]) per row, the out_proj input.
+ * Segment j covers rows [query_start_loc[j], query_start_loc[j+1]); it continues
+ * from cached state when has_initial_state[j] != 0 and writes its final windows /
+ * modal state into block state_indices[j * state_indices_stride].
+ */
+typedef struct hyena_prefill_args {
+  const void* z; int64_t ldz;   /* bf16, row stride in elements */
+  void* out; int64_t ldo;       /* bf16 */
+  int32_t T;                    /* rows available in z / out */
+  int32_t num_segments;
+  const int32_t* query_start_loc;      /* (num_segments + 1) device */
+  const uint8_t* has_initial_state;    /* (num_segments) device bool, or NULL = all fresh */
+  const int32_t* state_indices; int64_t state_indices_stride;
+  hyena_state_view conv_state;   /* S0 (bf16) */
+  hyena_state_view inner_state;  /* FIR: S1 (fp32); IIR: S2 (fp32, cols = modes) */
+  int32_t* error_flags;          /* optional device int */
+} hyena_prefill_args;
+
+HYENA_API size_t hyena_prefill_workspace_size(const hyena_layer_params* p, int32_t T,
+                                    int32_t num_segments);
+HYENA_API int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_args* a,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- decode / verify
+ * Replaces, for the decode rows of one step:
+ *   ordinary decode: triton_decode.hyena_decode (triton_decode.py:56-211) and the
+ *     unfused chain it stands for: vLLM causal_conv1d_update, _fir_decode_one /
+ *     _iir_decode_one -> triton_verifier.fir_one / iir_one (mixers.py:555-575,
+ *     1194-1205; triton_verifier.py:158-178);
+ *   speculative verify: the _short_conv spec branch (mixers.py:1153-1193),
+ *     _fir_decode_snapshots / _iir_decode_snapshots (mixers.py:578-663) ->
+ *     triton_verifier.fir_snapshots / iir_snapshots (triton_verifier.py:47-155).
+ * Request r owns tokens [token_start[r], token_start[r+1]) (NULL: token r only).
+ * The short window is read from conv_in_block[r] at column offset accepted[r]-1
+ * and the shifted window written to conv_out_block[r] (vLLM's spec convention).
+ * The inner state is read from in_slots[r, accepted[r]-1]; after token p the
+ * complete state snapshot is written to out_slots[r, p] (skipped for block 0 when
+ * skip_null_writes != 0, which is vLLM's null block).  Ordinary decode is q = 1,
+ * accepted = NULL (= 1) and in_slots == out_slots.  When zero_null_rows != 0 a
+ * request whose conv_in_block equals null_block writes a zero output row and no
+ * state (the fused-decode CUDA-graph padding rule, triton_decode.py:66-70).
+ */
+typedef struct hyena_decode_args {
+  const void* z; int64_t ldz;   /* (tokens, 3H) bf16 */
+  void* out; int64_t ldo;       /* (tokens, H) bf16 */
+  int32_t num_reqs;
+  int32_t q;                    /* max tokens per request (columns of in/out slots) */
+  const int32_t* token_start;   /* (num_reqs + 1) or NULL */
+  const int32_t* accepted;      /* (num_reqs) >= 1, or NULL */
+  const int32_t* conv_in_block; const int32_t* conv_out_block;  /* (num_reqs) */
+  const int32_t* in_slots; int64_t in_stride0, in_stride1;      /* (num_reqs, q) */
+  const int32_t* out_slots; int64_t out_stride0, out_stride1;   /* (num_reqs, q) */
+  int32_t zero_null_rows;
+  int32_t skip_null_writes;
+  int32_t null_block;
+  hyena_state_view conv_state;
+  hyena_state_view inner_state;
+  int32_t* error_flags;
+} hyena_decode_args;
+
+HYENA_API int hyena_decode(const hyena_layer_params* p, const hyena_decode_args* a, void* stream);
+
+/* ---------------------------------------------------------------- fp8 projection
+ * Static per-tensor E4M3 activation quantisation, q = e4m3_rn(clamp(x / sx, +-448)):
+ * the rule of fp8_emul.quantize_input (fp8_emul.py:76-78) and of vLLM's static
+ * W8A8 path the reference in_proj uses (mixers.py:740-757, 780-783).
+ * x: (M, K) bf16 with row stride ldx; q: (M, K) e4m3 contiguous rows of ldq.
+ */
+HYENA_API int hyena_quant_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, int32_t M,
+                     int32_t K, const float* input_scale, void* stream);
+
+/* out(M,N) bf16 = (A(M,K) e4m3 . B(N,K) e4m3^T) * (*scale_a) * (*scale_b):
+ * the in_proj GEMM (mixers.py:1076-1092 -> vLLM Fp8 ReplicatedLinear; numerics
+ * contract fp8_emul.py:81-88 with fp32 accumulation).  tcgen05 + TMA + TMEM.
+ * Requires K % 128 == 0, N % 8 == 0, 16-byte aligned rows. */
+HYENA_API int hyena_gemm_e4m3(const void* A, int64_t lda, const void* B, int64_t ldb,
+                    void* out, int64_t ldo, int32_t M, int32_t N, int32_t K,
+                    const float* scale_a, const float* scale_b, void* stream);
+
+/* out(M,N) bf16 = A(M,K) bf16 . B(N,K) bf16^T [+ bias(N)]: the out_proj GEMM
+ * (mixers.py:801-803, 1304, 1400 -> ReplicatedLinear with bias). tcgen05 + TMA.
+ * Requires K % 64 == 0, N % 8 == 0, 16-byte aligned rows. */
+HYENA_API int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
+                    void* out, int64_t ldo, int32_t M, int32_t N, int32_t K,
+                    const void* bias, void* stream);
+
+/* ---------------------------------------------------------------- misc */
+HYENA_API int hyena_abi_version(void);
+HYENA_API const char* hyena_last_error(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* HYENA_B200_H */

@@ -1,0 +1,77 @@
+"""The C-ABI library (CPU-side checks; nothing here launches a kernel):
+it loads, exports exactly the entry points include/hyena_b200.h declares, and
+rejects invalid arguments on the host before touching the device."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "hyena_b200.h").read_text()
+    return set(re.findall(r"HYENA_API\s+[\w\s\*]+?\b(hyena_\w+)\s*\(", text))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from evo2_flash_b200 import _build, _lib
+
+    _build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert {"hyena_prefill", "hyena_decode", "hyena_gemm_e4m3", "hyena_gemm_bf16",
+            "hyena_quant_e4m3", "hyena_prefill_workspace_size"} <= syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from evo2_flash_b200 import _lib
+
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.hyena_abi_version() == 1
+
+
+def test_invalid_arguments_are_rejected_on_host(lib):
+    from evo2_flash_b200._lib import LayerParams, PrefillArgs
+
+    p = LayerParams()
+    p.kind, p.H, p.K = 0, 100, 128  # H not a multiple of 64
+    a = PrefillArgs()
+    rc = lib.hyena_prefill(C.byref(p), C.byref(a), None, 0, None)
+    assert rc == 1
+    assert b"multiple of 64" in lib.hyena_last_error()
+    p.H, p.K = 128, 9  # unsupported taps
+    assert lib.hyena_prefill(C.byref(p), C.byref(a), None, 0, None) == 1
+    # null GEMM operands
+    assert lib.hyena_gemm_bf16(None, 64, None, 64, None, 64, 1, 8, 64, None, None) == 1
+
+
+def test_empty_work_is_a_no_op(lib):
+    from evo2_flash_b200._lib import LayerParams, PrefillArgs
+
+    p = LayerParams()
+    p.kind, p.H, p.K = 0, 128, 7
+    p.short_w = 1  # never dereferenced: no segments
+    p.inner_w = 1
+    a = PrefillArgs()
+    a.T, a.num_segments = 0, 0
+    assert lib.hyena_prefill(C.byref(p), C.byref(a), None, 0, None) == 0
+
+
+def test_workspace_size_only_for_li(lib):
+    from evo2_flash_b200._lib import LayerParams
+
+    p = LayerParams()
+    p.kind, p.H, p.K = 0, 4096, 128
+    assert lib.hyena_prefill_workspace_size(C.byref(p), 65536, 8) == 0
+    p.kind, p.K = 1, 16
+    n = lib.hyena_prefill_workspace_size(C.byref(p), 65536, 8)
+    assert n >= (65536 // 256) * 4096 * 16 * 4

@@ -1,0 +1,259 @@
+"""GPU parity of the sm_100a kernels, called through the C ABI (evo2_flash_b200.ops),
+against the CPU oracle on the same seeded inputs.
+
+Tolerance: the hot path's bar is max|a-b| / max|b| <= 2e-2 on bf16 outputs
+(REL_TOL); integer-valued / copied state (windows of bf16 inputs) must match
+bit for bit.
+"""
+
+import pytest
+import torch
+
+from oracle import hyena_oracle as O
+from tests.helpers import (REL_TOL, decode_meta, max_rel_err, params_to_oracle, prefill_meta,
+                           random_params)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _weights(p, kind):
+    from evo2_flash_b200 import ops
+
+    if kind == "hcl":
+        return ops.layer_weights("iir", p["short_filter"], D=p["D"], log_poles=p["log_poles"],
+                                 residues=p["residues"])
+    return ops.layer_weights("fir", p["short_filter"], conv=p["conv"], D=p.get("D"))
+
+
+def _random_states(H, num_blocks, W0, seed, spec_col=False):
+    g = torch.Generator().manual_seed(seed)
+    s0 = (torch.randn(num_blocks, W0, 3 * H, generator=g) * 0.3).to(torch.bfloat16)
+    s1 = torch.randn(num_blocks, 127, H, generator=g) * 0.1
+    s2 = torch.randn(num_blocks, H, 17 if spec_col else 16, generator=g)
+    return [s0, s1, s2]
+
+
+KINDS = [("hcs", 7), ("hcm", 128), ("hcl", 16)]
+
+
+@pytest.mark.parametrize("kind,k", KINDS)
+@pytest.mark.parametrize("layout", ["ragged", "long", "tiny"])
+def test_prefill_matches_oracle(kind, k, layout):
+    from evo2_flash_b200 import ops
+
+    H = 256
+    if layout == "ragged":
+        lengths, init = [700, 5, 131, 1, 1290, 64], [False, True, True, True, False, True]
+    elif layout == "long":
+        lengths, init = [3000, 1700], [True, False]
+    else:
+        lengths, init = [1, 2, 3, 126, 127, 128], [True] * 6
+    nb = len(lengths) + 2
+    blocks = list(range(2, 2 + len(lengths)))
+    p = random_params(kind, H, k, seed=11)
+    po = params_to_oracle(p, kind, H, k)
+    T = sum(lengths)
+    g = torch.Generator().manual_seed(12)
+    z = (torch.randn(T, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+    states = _random_states(H, nb, 2, seed=13)
+    ref_states = [s.clone() for s in states]
+    meta = prefill_meta(lengths, blocks, init)
+    ref = O.mixer_core(z, po, meta, ref_states, None, bf16_products=True)
+
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
+    dz = z.to(DEV)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    ds = [s.to(DEV) for s in states]
+    inner = ds[2] if kind == "hcl" else ds[1]
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dm = prefill_meta(lengths, blocks, init, device=DEV)
+    ops.prefill(w, dz, out, dm.query_start_loc_p, dm.has_initial_states_p, dm.state_indices_tensor_p,
+                ds[0], inner, error_flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    err = max_rel_err(out.cpu(), ref)
+    assert err < REL_TOL, err
+    assert torch.equal(ds[0].cpu(), ref_states[0])
+    if kind == "hcl":
+        assert max_rel_err(ds[2].cpu(), ref_states[2]) < 1e-4
+    else:
+        assert torch.equal(ds[1].cpu()[:, : k - 1], ref_states[1][:, : k - 1])
+        assert torch.equal(ds[1].cpu()[:, k - 1:], states[1][:, k - 1:])
+
+
+def test_hcl_prefill_against_float64_scan():
+    """Long segment: the chunked scan agrees with an exact float64 recurrence."""
+    from evo2_flash_b200 import ops
+
+    H, L = 128, 5000
+    p = random_params("hcl", H, 16, seed=21)
+    g = torch.Generator().manual_seed(22)
+    z = (torch.randn(L, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+    s_prev = torch.randn(H, 16, generator=g)
+    states = [torch.zeros(2, 2, 3 * H, dtype=torch.bfloat16), torch.zeros(2, 127, H),
+              torch.zeros(2, H, 16)]
+    states[2][1] = s_prev
+    meta = prefill_meta([L], [1], [True])
+    # u and x2 from the oracle's short filter, the LI map from the float64 scan
+    zf = O.short_fir_prefill(z, p["short_filter"].reshape(3 * H, 3), meta,
+                             states[0].clone(), True)
+    x2, x1, v = zf[:, 0::3], zf[:, 1::3], zf[:, 2::3]
+    u = x1 * v
+    y64, s64 = O.iir_segment_scan(u.float().t(), p["residues"], p["log_poles"][..., 0], s_prev)
+    y = y64.t().to(torch.bfloat16)
+    ref = (y + u * p["D"]) * x2
+
+    w = _weights({kk: vv.to(DEV) for kk, vv in p.items()}, "hcl")
+    out = torch.empty(L, H, dtype=torch.bfloat16, device=DEV)
+    ds = [s.to(DEV) for s in states]
+    dm = prefill_meta([L], [1], [True], device=DEV)
+    ops.prefill(w, z.to(DEV), out, dm.query_start_loc_p, dm.has_initial_states_p,
+                dm.state_indices_tensor_p, ds[0], ds[2])
+    torch.cuda.synchronize()
+    assert max_rel_err(out.cpu(), ref) < REL_TOL
+    assert max_rel_err(ds[2][1].cpu(), s64) < 1e-4
+
+
+@pytest.mark.parametrize("kind,k", KINDS)
+def test_decode_matches_oracle(kind, k):
+    from evo2_flash_b200 import ops
+
+    H, B = 256, 5
+    p = random_params(kind, H, k, seed=31)
+    po = params_to_oracle(p, kind, H, k)
+    states = _random_states(H, 8, 2, seed=32)
+    slots = [3, 1, 6, 2, 7]
+    g = torch.Generator().manual_seed(33)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
+    ds = [s.to(DEV) for s in states]
+    ref_states = [s.clone() for s in states]
+    for step in range(3):
+        z = (torch.randn(B, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+        meta = decode_meta(slots)
+        ref = O.mixer_core(z, po, meta, ref_states, None, bf16_products=True)
+        out = torch.empty(B, H, dtype=torch.bfloat16, device=DEV)
+        idx = torch.tensor(slots, dtype=torch.int32, device=DEV)
+        ops.decode(w, z.to(DEV), out, idx, idx, idx[:, None], idx[:, None], ds[0],
+                   ds[2] if kind == "hcl" else ds[1], zero_null_rows=True)
+        torch.cuda.synchronize()
+        assert max_rel_err(out.cpu(), ref) < REL_TOL
+    assert torch.equal(ds[0].cpu(), ref_states[0])
+    if kind == "hcl":
+        assert max_rel_err(ds[2].cpu(), ref_states[2]) < 1e-5
+    else:
+        assert torch.equal(ds[1].cpu()[:, : k - 1], ref_states[1][:, : k - 1])
+
+
+@pytest.mark.parametrize("kind,k", KINDS)
+def test_verify_matches_oracle(kind, k):
+    """Speculative verify: q=4, ragged lengths, accepted counts 1..4, snapshots."""
+    from evo2_flash_b200 import ops
+
+    H = 256
+    p = random_params(kind, H, k, seed=41)
+    po = params_to_oracle(p, kind, H, k)
+    slots = [[1, 5, 6, 7], [2, 8, 9, 10], [3, 11, 12, 13]]
+    lengths = [4, 2, 1]
+    accepted = torch.tensor([1, 3, 4])
+    states = _random_states(H, 14, 5, seed=42, spec_col=True)
+    ref_states = [s.clone() for s in states]
+    T = sum(lengths)
+    g = torch.Generator().manual_seed(43)
+    z = (torch.randn(T, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+    meta = decode_meta(slots, lengths, computed=[10, 20, 30])
+    ref = O.mixer_core(z, po, meta, ref_states, accepted, bf16_products=True)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
+    ds = [s.to(DEV) for s in states]
+    st = torch.tensor(slots, dtype=torch.int32, device=DEV)
+    qs = torch.tensor([0, 4, 6, 7], dtype=torch.int32, device=DEV)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    ops.decode(w, z.to(DEV), out, st[:, 0], st[:, 0], st, st, ds[0],
+               ds[2] if kind == "hcl" else ds[1], token_start=qs, accepted=accepted.to(DEV))
+    torch.cuda.synchronize()
+    assert max_rel_err(out.cpu(), ref) < REL_TOL
+    assert torch.equal(ds[0].cpu()[1:], ref_states[0][1:])
+    if kind == "hcl":
+        assert max_rel_err(ds[2].cpu()[1:, :, :16], ref_states[2][1:, :, :16]) < 1e-5
+    else:
+        assert torch.equal(ds[1].cpu()[1:, : k - 1], ref_states[1][1:, : k - 1])
+
+
+def test_decode_null_block_row_is_zero_and_writes_nothing():
+    from evo2_flash_b200 import ops
+
+    H = 128
+    p = random_params("hcm", H, 128, seed=51)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, "hcm")
+    states = [s.to(DEV) for s in _random_states(H, 4, 2, seed=52)]
+    before = [s.clone() for s in states]
+    z = torch.randn(2, 3 * H, device=DEV).to(torch.bfloat16)
+    out = torch.full((2, H), 7.0, dtype=torch.bfloat16, device=DEV)
+    idx = torch.tensor([0, 2], dtype=torch.int32, device=DEV)
+    ops.decode(w, z, out, idx, idx, idx[:, None], idx[:, None], states[0], states[1],
+               zero_null_rows=True)
+    torch.cuda.synchronize()
+    assert torch.all(out[0] == 0)
+    assert torch.equal(states[0][0], before[0][0]) and torch.equal(states[1][0], before[1][0])
+    assert not torch.equal(states[1][2], before[1][2])
+
+
+def test_out_of_range_block_sets_flag_without_fault():
+    from evo2_flash_b200 import ops
+
+    H = 128
+    p = random_params("hcs", H, 7, seed=61)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, "hcs")
+    states = [s.to(DEV) for s in _random_states(H, 3, 2, seed=62)]
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    z = torch.randn(10, 3 * H, device=DEV).to(torch.bfloat16)
+    out = torch.empty(10, H, dtype=torch.bfloat16, device=DEV)
+    m = prefill_meta([10], [99], [True], device=DEV)
+    ops.prefill(w, z, out, m.query_start_loc_p, m.has_initial_states_p, m.state_indices_tensor_p,
+                states[0], states[1], error_flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) & 1
+
+
+def test_quant_e4m3_exact():
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(71)
+    x = (torch.randn(300, 512, generator=g) * 3).to(torch.bfloat16)
+    sx = torch.tensor([0.01], dtype=torch.float32)
+    ref = O.quantize_input(x, sx)
+    q = ops.quant_e4m3(x.to(DEV), sx.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(q.float().cpu(), ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
+                                   (4096, 12288, 4096)])
+def test_gemm_e4m3(M, N, K):
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(M + N)
+    a = (torch.randn(M, K, generator=g) * 4).to(torch.float8_e4m3fn)
+    b = (torch.randn(N, K, generator=g) * 4).to(torch.float8_e4m3fn)
+    sa = torch.tensor([0.02], dtype=torch.float32)
+    sb = torch.tensor([0.003], dtype=torch.float32)
+    da, db = a.to(DEV), b.to(DEV)
+    out = ops.gemm_e4m3(da, db, sa.to(DEV), sb.to(DEV))
+    ref = ((da.float() @ db.float().t()) * sa.to(DEV) * sb.to(DEV)).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert max_rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 512), (1000, 776, 192),
+                                   (4096, 4096, 4096)])
+def test_gemm_bf16_bias(M, N, K):
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 3 + N)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    b = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    bias = torch.randn(N, generator=g).to(torch.bfloat16).to(DEV)
+    out = ops.gemm_bf16(a, b, bias)
+    ref = (a.float() @ b.float().t() + bias.float()).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert max_rel_err(out, ref) < 1e-2
