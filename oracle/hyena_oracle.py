@@ -389,17 +389,18 @@ def mixer_core(z, p, meta, states, accepted=None, bf16_products=True):
 
 
 def in_proj(x, p, hopper=False):
+    """fp8 static W8A8 (fp8_emul.py:81-88) or, for bf16 weights, the reference's
+    CPU projection: F.linear in the activation dtype (ReplicatedLinear)."""
     if getattr(p, "in_proj_scales", None) is not None:
         sx, sw = p.in_proj_scales
         return fp8_linear(x, p.in_proj_weight, sx, sw, hopper=hopper)
-    return (x.float() @ p.in_proj_weight.float().t()).to(x.dtype)
+    return F.linear(x, p.in_proj_weight.to(x.dtype))
 
 
 def out_proj(g, p):
-    y = g.float() @ p.out_proj_weight.float().t()
-    if p.out_proj_bias is not None:
-        y = y + p.out_proj_bias.float()
-    return y.to(g.dtype)
+    """out_proj with bias (mixers.py:801-803): F.linear in the activation dtype."""
+    b = None if p.out_proj_bias is None else p.out_proj_bias.to(g.dtype)
+    return F.linear(g, p.out_proj_weight.to(g.dtype), b)
 
 
 def mixer_forward(x, p, meta, states, accepted=None, bf16_products=True, hopper=False):

@@ -51,7 +51,9 @@ def test_mixer_replays_reference(name):
     got = [s.cpu() for s in m.kv_cache]
     assert torch.equal(got[0][1:], ref[0][1:])
     if fx["kind"] == "hcl":
-        assert max_rel_err(got[2][1:, :, :16], ref[2][1:, :, :16]) < 1e-3
+        # the fixture's prefill K=3 filter uses fp32 products (the reference's CPU
+        # twin), this path bf16 ones (its GPU kernel): u differs in the last bit
+        assert max_rel_err(got[2][1:, :, :16], ref[2][1:, :, :16]) < REL_TOL
     else:
         k = fx["k_inner"]
         assert max_rel_err(got[1][1:, : k - 1], ref[1][1:, : k - 1]) < 1e-2
