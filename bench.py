@@ -416,6 +416,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", choices=["prefill", "decode"], default=None,
+                    help="run one workload (small profiling cases)")
+    ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per rank")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -456,12 +459,19 @@ def main():
 
     gen = torch.Generator().manual_seed(1234 + rank)
     table = torch.randn(512, H, generator=torch.Generator().manual_seed(1))
-    T = PREFILL_B * PREFILL_L
+    T = args.batch * PREFILL_L
     x = embed_norm(acgt_tokens(T, gen), table, device)
     calib = embed_norm(acgt_tokens(4096, torch.Generator().manual_seed(9)), table, device)
     input_scale = (calib.float().abs().amax() / 448.0).reshape(1).cpu()
     layers = build_triple(device, input_scale, num_blocks=DECODE_B + 2)
-    meta = prefill_meta([PREFILL_L] * PREFILL_B, list(range(1, PREFILL_B + 1)), device)
+    meta = prefill_meta([PREFILL_L] * args.batch, list(range(1, args.batch + 1)), device)
+
+    if args.only == "decode":  # decode-only profiling case
+        dgen = torch.Generator().manual_seed(2 + rank)
+        d_ms, _ = run_decode(layers, table, device, args.decode_steps, args.warmup, dgen)
+        if rank == 0:
+            print(json.dumps({"decode_ms_per_step": d_ms, "decode_tok_per_s": DECODE_B / d_ms * 1e3}))
+        return
 
     with KernelTimer(ops_mod, "gemm_e4m3") as gt:
         ms, clocks = run_prefill(layers, x, meta, args.steps, args.warmup, dist_ok, device, gt)
@@ -484,7 +494,7 @@ def main():
                   + b_quant / (hbm * 1e9) + b_core / (hbm * 1e9))
 
     decode = None
-    if not os.environ.get("HYENA_BENCH_NO_DECODE"):
+    if args.only != "prefill" and not os.environ.get("HYENA_BENCH_NO_DECODE"):
         dgen = torch.Generator().manual_seed(2 + rank)
         d_ms, lengths = run_decode(layers, table, device, args.decode_steps, args.warmup, dgen)
         if dist_ok:
@@ -526,7 +536,7 @@ def main():
         "data": "synthetic (seeded ACGT, random-init weights)",
         "config": {"workload": "config2: HCS+HCM+HCL mixer triple prefill, 7B shape",
                    "model": "StripedHyena2-7B mixer triple (random init)", "hidden": H,
-                   "global_batch": PREFILL_B * world, "seq_len": PREFILL_L,
+                   "global_batch": args.batch * world, "seq_len": PREFILL_L,
                    "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (x 512 MiB, z 1.5 GiB per layer)"},
         "roofline": {"bound": "tensor", "kernel": "hyena_gemm_e4m3 (in_proj, tcgen05)",
                      "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",

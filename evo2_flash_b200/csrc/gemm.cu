@@ -156,7 +156,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  // N is the fastest grid dimension: CTAs resident together share one A row
+  // panel, and the whole weight (<= 50 MB at the 7B shape) stays in L2 while the
+  // activations stream through once.
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   constexpr int ELEM = FP8 ? 1 : 2;
   constexpr int KE = BKB / ELEM;  // K elements per stage
   const int kblocks = K / KE;
@@ -326,7 +329,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
       return check_launch("cudaFuncSetAttribute(gemm)");
     attr = true;
   }
-  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
   gemm_kernel<FP8><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N, K,
                                                 sa, sb, static_cast<const bf16*>(bias));
   return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
