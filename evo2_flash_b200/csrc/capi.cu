@@ -82,6 +82,8 @@ int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_args* a, void
   HB_REQUIRE(a->z && a->out && a->query_start_loc && a->state_indices, "null prefill pointer");
   HB_REQUIRE(aligned16(a->z) && a->ldz % 8 == 0, "z must be 16-byte aligned with ldz % 8 == 0");
   HB_REQUIRE(a->ldz >= 3LL * p->H && a->ldo >= p->H, "row strides too small");
+  HB_REQUIRE((reinterpret_cast<uintptr_t>(a->out) & 3u) == 0 && a->ldo % 2 == 0,
+             "out must be 4-byte aligned with an even row stride");
   if ((rc = check_view(a->conv_state, "conv_state", 2))) return rc;
   if (p->kind == HYENA_KIND_FIR) {
     if ((rc = check_view(a->inner_state, "inner_state", p->K - 1))) return rc;

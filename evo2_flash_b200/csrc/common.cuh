@@ -69,6 +69,53 @@ __device__ __forceinline__ float modal_readout16(const float* s, const float* r)
   return add_rn(p[0], p[1]);
 }
 
+// ---------------------------------------------------------------- packed math
+// bf16x2 / f32x2 helpers.  A bf16x2 product is the correctly rounded bf16 of
+// the exact product (the rounding a torch bf16 multiply performs), and a bf16x2
+// sum of two bf16 values equals torch's fp32-add-then-round (the exact sum of
+// two bf16 numbers either fits fp32 or the smaller term is below half an ulp).
+typedef __nv_bfloat162 bf162;
+
+__device__ __forceinline__ bf162 as_bf162(uint32_t v) { return *reinterpret_cast<bf162*>(&v); }
+__device__ __forceinline__ uint32_t as_u32(bf162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// (lo, hi) of a bf16x2 as fp32
+__device__ __forceinline__ float2 unpack2(bf162 v) { return __bfloat1622float2(v); }
+
+__device__ __forceinline__ bf162 pack2_rn(float2 v) { return __floats2bfloat162_rn(v.x, v.y); }
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long ra, rb, rc;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rc) : "l"(ra), "l"(rb));
+  float2 c;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(c.x), "=f"(c.y) : "l"(rc));
+  return c;
+}
+
+// c + a * b, elementwise on two fp32 lanes, one rounding each (fmaf per lane).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long ra, rb, rc, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+
+// short_tap on a channel pair: products rounded to bf16 (bf16x2 multiply),
+// summed oldest first in fp32, result rounded to bf16.
+__device__ __forceinline__ bf162 short_tap2(bf162 c0, bf162 c1, bf162 x, bf162 w0, bf162 w1,
+                                            bf162 w2) {
+  const float2 p0 = unpack2(__hmul2(c0, w0));
+  const float2 p1 = unpack2(__hmul2(c1, w1));
+  const float2 p2 = unpack2(__hmul2(x, w2));
+  return pack2_rn(fadd2(fadd2(p0, p1), p2));
+}
+
 // Largest j with qsl[j] <= row, for a non-decreasing qsl[0..n].
 __device__ __forceinline__ int find_segment(const int32_t* qsl, int n, int row) {
   int lo = 0, hi = n;  // invariant: answer in [lo, hi)

@@ -222,9 +222,265 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   }
 }
 
+// ---------------------------------------------------------------- q = 1 fast path
+// Ordinary decode (one token per request, accepted = 1, a 2-column short window
+// with unit channel stride): a thread owns 4 consecutive channels (FIR) or one
+// channel's 16 modes (IIR) and streams its state with 16-byte accesses, 16 taps in
+// flight.  Same arithmetic, order and rounding as decode_kernel.
+constexpr int FAST_THREADS = 128;
+
+__device__ __forceinline__ void load_bf16x4(const bf16* p, float (&v)[4]) {
+  const uint2 r = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+  v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
+}
+
+__device__ __forceinline__ void store_bf16x4(bf16* p, const float (&v)[4]) {
+  uint2 r;
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+  r.x = *reinterpret_cast<const uint32_t*>(&a);
+  r.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = r;
+}
+
+// Short filter + gate for `C` consecutive channels starting at h: reads the
+// triple row of z and window columns 0, 1 of S0 (block cin), writes [c1, x] to
+// block cout.  Returns x2 and u per channel.
+template <int C>
+__device__ __forceinline__ void short_gate_q1(const hyena_layer_params& P,
+                                              const hyena_decode_args& A, int t0, int h,
+                                              long long cin, long long cout, bool write_conv,
+                                              float (&x2)[C], float (&u)[C]) {
+  const bf16* z = static_cast<const bf16*>(A.z) + (long long)t0 * A.ldz + 3 * h;
+  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const bf16* c0p = s0 + cin * A.conv_state.block_stride + 3 * h;
+  const bf16* c1p = c0p + A.conv_state.col_stride;
+  const bf16* sw = static_cast<const bf16*>(P.short_w) + 9 * h;
+  float zx[3 * C], w0[3 * C], w1[3 * C];
+#pragma unroll
+  for (int i = 0; i < 3 * C; i += 4) {
+    float a[4], b[4];
+    load_bf16x4(z + i, a);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) zx[i + k] = a[k];
+    load_bf16x4(c0p + i, a);
+    load_bf16x4(c1p + i, b);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { w0[i + k] = a[k]; w1[i + k] = b[k]; }
+  }
+  float o[3 * C];
+#pragma unroll
+  for (int i = 0; i < 3 * C; ++i)
+    o[i] = short_tap(w0[i], w1[i], zx[i], ldbf(sw + 3 * i), ldbf(sw + 3 * i + 1), ldbf(sw + 3 * i + 2));
+  if (write_conv) {
+    bf16* d0 = s0 + cout * A.conv_state.block_stride + 3 * h;
+    bf16* d1 = d0 + A.conv_state.col_stride;
+#pragma unroll
+    for (int i = 0; i < 3 * C; i += 4) {
+      float a[4] = {w1[i], w1[i + 1], w1[i + 2], w1[i + 3]};
+      float b[4] = {zx[i], zx[i + 1], zx[i + 2], zx[i + 3]};
+      store_bf16x4(d0 + i, a);
+      store_bf16x4(d1 + i, b);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    x2[c] = o[3 * c];
+    u[c] = bf16r(o[3 * c + 1] * o[3 * c + 2]);
+  }
+}
+
+template <int K>
+__global__ void __launch_bounds__(FAST_THREADS)
+decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  constexpr int HIST = K - 1;
+  constexpr int U = 16;  // taps in flight
+  const int r = blockIdx.x;
+  const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
+  if (h >= P.H) return;
+  const long long cin = __ldg(A.conv_in_block + r);
+  const long long cout = __ldg(A.conv_out_block + r);
+  bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo + h;
+  if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
+    if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
+      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    store_bf16x4(out, zero);
+    return;
+  }
+  const bool write_conv = block_ok(cout, A.conv_state) &&
+                          !(A.skip_null_writes && cout == A.null_block);
+  float x2[4], u[4];
+  short_gate_q1<4>(P, A, r, h, cin, cout, write_conv, x2, u);
+
+  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
+  const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
+  const bool src_ok = block_ok(src, A.inner_state);
+  const bool dok = block_ok(dst, A.inner_state) && !(A.skip_null_writes && dst == A.null_block);
+  if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+  float* st = static_cast<float*>(A.inner_state.data);
+  const long long cs = A.inner_state.col_stride;
+  const float* sp = st + (src_ok ? src : 0) * A.inner_state.block_stride + h;
+  float* dp = st + (dok ? dst : 0) * A.inner_state.block_stride + h;
+  const bf16* w = static_cast<const bf16*>(P.inner_w) + h;  // (K, H) layout, unit channel stride
+  const long long wk = P.inner_w_stride_k;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int k0 = 0; k0 < HIST; k0 += U) {
+    float4 sv[U];
+    float wv[U][4];
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      if (k0 + t < HIST) {
+        sv[t] = src_ok ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + t) * cs)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        load_bf16x4(w + (long long)(k0 + t) * wk, wv[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      if (k0 + t < HIST) {
+        acc[0] = fmaf(wv[t][0], sv[t].x, acc[0]);
+        acc[1] = fmaf(wv[t][1], sv[t].y, acc[1]);
+        acc[2] = fmaf(wv[t][2], sv[t].z, acc[2]);
+        acc[3] = fmaf(wv[t][3], sv[t].w, acc[3]);
+        if (dok && k0 + t >= 1) *reinterpret_cast<float4*>(dp + (long long)(k0 + t - 1) * cs) = sv[t];
+      }
+    }
+  }
+  float wl[4];
+  load_bf16x4(w + (long long)HIST * wk, wl);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) acc[c] = fmaf(wl[c], u[c], acc[c]);
+  if (dok) *reinterpret_cast<float4*>(dp + (long long)(HIST - 1) * cs) = make_float4(u[0], u[1], u[2], u[3]);
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  if (Dg) load_bf16x4(Dg + h, d);
+  float g[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float yy = bf16r(acc[c]);
+    if (Dg) yy = bf16r(yy + bf16r(d[c] * u[c]));
+    g[c] = bf16r(x2[c] * yy);
+  }
+  store_bf16x4(out, g);
+}
+
+__global__ void __launch_bounds__(FAST_THREADS)
+decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  const int r = blockIdx.x;
+  const int h = blockIdx.y * FAST_THREADS + threadIdx.x;
+  if (h >= P.H) return;
+  const long long cin = __ldg(A.conv_in_block + r);
+  const long long cout = __ldg(A.conv_out_block + r);
+  bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo + h;
+  if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
+    if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
+      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+    *out = __float2bfloat16_rn(0.0f);
+    return;
+  }
+  const bool write_conv = block_ok(cout, A.conv_state) &&
+                          !(A.skip_null_writes && cout == A.null_block);
+  // one channel: scalar short filter
+  const bf16* z = static_cast<const bf16*>(A.z) + (long long)r * A.ldz + 3 * h;
+  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const bf16* sw = static_cast<const bf16*>(P.short_w) + 9 * h;
+  float o[3];
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    const long long base = cin * A.conv_state.block_stride + 3 * h + q;
+    const float c0 = ldbf(s0 + base), c1 = ldbf(s0 + base + A.conv_state.col_stride);
+    const float x = ldbf(z + q);
+    o[q] = short_tap(c0, c1, x, ldbf(sw + 3 * q), ldbf(sw + 3 * q + 1), ldbf(sw + 3 * q + 2));
+    if (write_conv) {
+      const long long ob = cout * A.conv_state.block_stride + 3 * h + q;
+      s0[ob] = __float2bfloat16_rn(c1);
+      s0[ob + A.conv_state.col_stride] = __float2bfloat16_rn(x);
+    }
+  }
+  const float u = bf16r(o[1] * o[2]);
+  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
+  const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
+  const bool src_ok = block_ok(src, A.inner_state);
+  const bool dok = block_ok(dst, A.inner_state) && !(A.skip_null_writes && dst == A.null_block);
+  if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+  float* st = static_cast<float*>(A.inner_state.data);
+  const float4* sp = reinterpret_cast<const float4*>(
+      st + (src_ok ? src : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
+  float4* dp = reinterpret_cast<float4*>(
+      st + (dok ? dst : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
+  float s[16], pl[16], rs[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = src_ok ? sp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s[4 * q] = v.x; s[4 * q + 1] = v.y; s[4 * q + 2] = v.z; s[4 * q + 3] = v.w;
+  }
+  const float* lp = P.log_poles + (long long)h * P.lp_stride_h;
+  const float* rr = P.residues + (long long)h * P.res_stride_h;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    pl[q] = expf(lp[q * P.lp_stride_s]);
+    rs[q] = rr[q * P.res_stride_s];
+  }
+#pragma unroll
+  for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u);
+  if (dok) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dp[q] = make_float4(s[4 * q], s[4 * q + 1], s[4 * q + 2], s[4 * q + 3]);
+  }
+  float y = bf16r(modal_readout16(s, rs));
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  if (Dg) y = bf16r(y + bf16r(ldbf(Dg + h) * u));
+  *out = __float2bfloat16_rn(bf16r(o[0] * y));
+}
+
+static bool aligned_elems(const void* p, int64_t stride_elems, int elem_bytes, int vec_bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % vec_bytes) == 0 &&
+         (stride_elems * elem_bytes) % vec_bytes == 0;
+}
+
+// The q = 1 kernels apply when each request has exactly one token, no accepted
+// offsets, a 2-column short window, unit channel strides and 16-byte-aligned rows.
+static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
+  if (A.q != 1 || A.token_start != nullptr || A.accepted != nullptr) return false;
+  if (A.conv_state.cols != 2 || A.conv_state.dim_stride != 1) return false;
+  if (!aligned_elems(A.z, A.ldz, 2, 8) || !aligned_elems(A.out, A.ldo, 2, 8)) return false;
+  if (!aligned_elems(A.conv_state.data, A.conv_state.block_stride, 2, 8) ||
+      (A.conv_state.col_stride * 2) % 8 != 0)
+    return false;
+  const hyena_state_view& s = A.inner_state;
+  if (P.kind == HYENA_KIND_FIR) {
+    if (s.dim_stride != 1 || P.inner_w_stride_h != 1 || (P.inner_w_stride_k * 2) % 8 != 0) return false;
+    if (!aligned_elems(P.inner_w, 0, 2, 8) || (P.D && !aligned_elems(P.D, 0, 2, 8))) return false;
+    return aligned_elems(s.data, s.block_stride, 4, 16) && (s.col_stride * 4) % 16 == 0 &&
+           P.H % 4 == 0;
+  }
+  return s.col_stride == 1 && aligned_elems(s.data, s.block_stride, 4, 16) &&
+         (s.dim_stride * 4) % 16 == 0;
+}
+
 int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaStream_t st) {
   if (A.conv_state.cols > DEC_MAXW0)
     return fail(HYENA_ERR_UNSUPPORTED, "conv window wider than 8 columns");
+  if (fast_path_ok(P, A)) {
+    if (P.kind == HYENA_KIND_IIR && P.K == 16) {
+      dim3 g(A.num_reqs, (P.H + FAST_THREADS - 1) / FAST_THREADS);
+      decode_iir_q1_kernel<<<g, FAST_THREADS, 0, st>>>(P, A);
+      return check_launch("decode_iir_q1_kernel");
+    }
+    dim3 g(A.num_reqs, (P.H / 4 + FAST_THREADS - 1) / FAST_THREADS);
+    if (P.kind == HYENA_KIND_FIR && P.K == 128) {
+      decode_fir_q1_kernel<128><<<g, FAST_THREADS, 0, st>>>(P, A);
+      return check_launch("decode_fir_q1_kernel<128>");
+    }
+    if (P.kind == HYENA_KIND_FIR && P.K == 7) {
+      decode_fir_q1_kernel<7><<<g, FAST_THREADS, 0, st>>>(P, A);
+      return check_launch("decode_fir_q1_kernel<7>");
+    }
+  }
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
   if (P.kind == HYENA_KIND_IIR) {
     if (P.K != 16) return fail(HYENA_ERR_UNSUPPORTED, "IIR decode supports modal order 16");

@@ -22,21 +22,28 @@ namespace hb {
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BKB = 128;  // bytes of K per stage (one 128B swizzle row)
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BKB;
-constexpr int B_BYTES = BN * BKB;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;
 constexpr unsigned long long WAIT_BUDGET_NS = 4000000000ull;  // 4 s
 
+// Tile configuration for an N-tile of BN columns: as many pipeline stages as
+// fit in ~192 KB of shared memory (4 at BN = 256, 8 at BN <= 64), and a TMEM
+// accumulator of BN fp32 columns.
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BKB;
+  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+};
+
+template <int BN>
 struct __align__(1024) Smem {
-  uint8_t a[STAGES][A_BYTES];
-  uint8_t b[STAGES][B_BYTES];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint8_t a[Cfg<BN>::STAGES][Cfg<BN>::A_BYTES];
+  uint8_t b[Cfg<BN>::STAGES][Cfg<BN>::B_BYTES];
+  uint64_t full[Cfg<BN>::STAGES];
+  uint64_t empty[Cfg<BN>::STAGES];
   uint64_t tmem_full;
   uint32_t tmem_base;
 };
@@ -140,21 +147,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 // Instruction descriptor: fp32 accumulator, K-major A and B, M=128, N=256;
 // operand format E4M3 (kind::f8f6f4) or BF16 (kind::f16).
-template <bool FP8>
+template <bool FP8, int BN>
 __host__ __device__ constexpr uint32_t idesc() {
   return (1u << 4) | ((FP8 ? 0u : 1u) << 7) | ((FP8 ? 0u : 1u) << 10) |
          (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 }
 
-template <bool FP8>
+template <bool FP8, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
             const float* __restrict__ sa, const float* __restrict__ sb,
             const bf16* __restrict__ bias) {
+  constexpr int STAGES = Cfg<BN>::STAGES;
+  constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = Cfg<BN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
-  Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                     ~uintptr_t(1023));
+  Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   // N is the fastest grid dimension: CTAs resident together share one A row
   // panel, and the whole weight (<= 50 MB at the 7B shape) stays in L2 while the
@@ -204,7 +214,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t ID = idesc<FP8>();
+      constexpr uint32_t ID = idesc<FP8, BN>();
       for (int kb = 0; kb < kblocks; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
@@ -305,6 +315,37 @@ static int make_map(CUtensorMap* m, const void* base, bool fp8, uint64_t inner, 
   return HYENA_OK;
 }
 
+template <bool FP8, int BN>
+static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* out, int64_t ldo,
+                     int M, int N, int K, const float* sa, const float* sb, const void* bias,
+                     cudaStream_t st) {
+  CUtensorMap tb;
+  int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
+  if (rc) return rc;
+  const size_t smem = sizeof(Smem<BN>) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_kernel<FP8, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return check_launch("cudaFuncSetAttribute(gemm)");
+    attr = true;
+  }
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
+                                                    K, sa, sb, static_cast<const bf16*>(bias));
+  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+}
+
+// N-tile choice: the widest tile that still gives at least one CTA per SM
+// (148 on B200); small-M (decode) GEMMs get narrow tiles and more CTAs.
+static int pick_bn(int M, int N) {
+  const long long mt = (M + BM - 1) / BM;
+  for (int bn : {256, 128, 64}) {
+    if (mt * ((N + bn - 1) / bn) >= 148) return bn;
+  }
+  return 32;
+}
+
 template <bool FP8>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out, int64_t ldo,
                   int M, int N, int K, const float* sa, const float* sb, const void* bias,
@@ -317,22 +358,15 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   HB_REQUIRE((lda * (FP8 ? 1 : 2)) % 16 == 0 && (ldb * (FP8 ? 1 : 2)) % 16 == 0,
              "GEMM row strides must be multiples of 16 bytes");
   HB_REQUIRE(lda >= K && ldb >= K && ldo >= N, "GEMM leading dimensions too small");
-  CUtensorMap ta, tb;
+  CUtensorMap ta;
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
-  if ((rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN))) return rc;
-  const size_t smem = sizeof(Smem) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemm_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(gemm)");
-    attr = true;
+  switch (pick_bn(M, N)) {
+    case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
   }
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  gemm_kernel<FP8><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N, K,
-                                                sa, sb, static_cast<const bf16*>(bias));
-  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
 }
 
 }  // namespace gemm

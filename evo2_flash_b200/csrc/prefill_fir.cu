@@ -20,9 +20,10 @@
 namespace hb {
 
 constexpr int FIR_CG = 64;       // channels per CTA
+constexpr int FIR_PAIRS = FIR_CG / 2;
 constexpr int FIR_BT = 64;       // rows per tile
 constexpr int FIR_THREADS = 256;
-constexpr int FIR_RPT = 16;      // output rows per thread in the tap loop
+constexpr int FIR_RPT = 8;       // rows per thread in the gate and tap phases
 constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
 
 template <int K>
@@ -31,22 +32,18 @@ struct FirCfg {
   static constexpr int RING = ((HIST + FIR_BT + 15) / 16) * 16;
 };
 
+// Thread (pair p = tid % 32, row group g = tid / 32) owns channels c0+2p, c0+2p+1
+// and tile rows 8g .. 8g+7 in both the gate and the tap phases.
 template <int K>
 struct FirShared {
-  float ring[FirCfg<K>::RING][FIR_CG];  // u by row (mod RING), fp32 (state values are fp32)
-  bf16 zt[FIR_BT][3 * FIR_CG];          // z tile
-  bf16 x2s[FIR_BT][FIR_CG];             // x2 of the tile
-  bf16 wsm[K][FIR_CG];                  // inner taps, [k][c]
-  float zh[2][3 * FIR_CG];              // z rows (r-2, r-1) before the tile
-  float sw[3][3 * FIR_CG];              // short taps [tap][col]
-  float dsm[FIR_CG];
+  float2 ring[FirCfg<K>::RING][FIR_PAIRS];  // u by row (mod RING), fp32 pairs
+  uint32_t zt[FIR_BT][3 * FIR_PAIRS];       // z tile, raw bf16x2 words
+  bf162 x2s[FIR_BT][FIR_PAIRS];             // x2 of the tile
+  bf162 wsm[K][FIR_PAIRS];                  // inner taps, [k][pair]
+  uint32_t zh[2][3 * FIR_PAIRS];            // z rows (r-2, r-1) before the tile
+  bf162 sw[3][3][FIR_PAIRS];                // short taps [column x2/x1/v][tap][pair]
+  bf162 dsm[FIR_PAIRS];
 };
-
-template <int RING>
-__device__ __forceinline__ int ring_idx(long long t) {
-  long long m = t % RING;
-  return int(m < 0 ? m + RING : m);
-}
 
 struct SegCtx {
   int a, e;       // segment rows
@@ -92,6 +89,19 @@ __device__ __forceinline__ float u_at(const hyena_prefill_args& A, const hyena_l
   return bf16r(val[0] * val[1]);
 }
 
+__device__ __forceinline__ uint32_t bf16_bits(float v) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// The interleaved triple words of one channel pair -> (x2, x1, v) bf16x2 pairs.
+// Words: w0 = (x2_a, x1_a), w1 = (v_a, x2_b), w2 = (x1_b, v_b).
+__device__ __forceinline__ void split_triples(uint32_t w0, uint32_t w1, uint32_t w2, bf162& x2,
+                                              bf162& x1, bf162& v) {
+  x2 = as_bf162(__byte_perm(w0, w1, 0x7610));
+  x1 = as_bf162(__byte_perm(w0, w2, 0x5432));
+  v = as_bf162(__byte_perm(w1, w2, 0x7610));
+}
+
 template <int K>
 __global__ void __launch_bounds__(FIR_THREADS, 2)
 fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
@@ -116,19 +126,26 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float* s1 = static_cast<const float*>(A.inner_state.data);
 
-  for (int i = tid; i < K * FIR_CG; i += FIR_THREADS) {
-    const int k = i / FIR_CG, c = i % FIR_CG;
-    S.wsm[k][c] = iw[(long long)(c0 + c) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k];
+  for (int i = tid; i < K * FIR_PAIRS; i += FIR_THREADS) {
+    const int k = i / FIR_PAIRS, pp = i % FIR_PAIRS;
+    const long long h = c0 + 2 * pp;
+    S.wsm[k][pp] = __halves2bfloat162(iw[h * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k],
+                                      iw[(h + 1) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]);
   }
-  for (int i = tid; i < 9 * FIR_CG; i += FIR_THREADS) {
-    const int col = i / 3, tap = i % 3;
-    S.sw[tap][col] = ldbf(swg + (long long)(3 * c0 + col) * 3 + tap);
+  for (int i = tid; i < 9 * FIR_PAIRS; i += FIR_THREADS) {
+    const int col = i / (3 * FIR_PAIRS), tap = (i / FIR_PAIRS) % 3, pp = i % FIR_PAIRS;
+    const long long h = c0 + 2 * pp;
+    S.sw[col][tap][pp] = __halves2bfloat162(swg[(3 * h + col) * 3 + tap],
+                                            swg[(3 * (h + 1) + col) * 3 + tap]);
   }
-  if (tid < FIR_CG) S.dsm[tid] = Dg ? ldbf(Dg + c0 + tid) : 0.0f;
+  if (tid < FIR_PAIRS)
+    S.dsm[tid] = Dg ? __halves2bfloat162(Dg[c0 + 2 * tid], Dg[c0 + 2 * tid + 1])
+                    : __floats2bfloat162_rn(0.f, 0.f);
   __syncthreads();
 
-  const int c = tid % FIR_CG;  // channel of this thread in the gate / FIR phases
-  const int rl = tid / FIR_CG; // 0..3
+  const int pp = tid % FIR_PAIRS;  // channel pair
+  const int rg = tid / FIR_PAIRS;  // row group 0..7
+  float* ring_f = reinterpret_cast<float*>(&S.ring[0][0]);
 
   int r = r0;
   int j = find_segment(qsl, nseg, r);
@@ -157,11 +174,16 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
       } else {
         val = 0.0f;
       }
-      S.ring[ring_idx<RING>(t)][cc] = val;
+      int ri = (int)(t % RING);
+      ri += ri < 0 ? RING : 0;
+      ring_f[ri * FIR_CG + cc] = val;
     }
-    for (int i = tid; i < 2 * 3 * FIR_CG; i += FIR_THREADS) {
-      const int q = i / (3 * FIR_CG), col = i % (3 * FIR_CG);
-      S.zh[q][col] = z_at(A, seg, (long long)r - 2 + q, 3 * c0 + col);
+    for (int i = tid; i < 2 * 3 * FIR_PAIRS; i += FIR_THREADS) {
+      const int q = i / (3 * FIR_PAIRS), wd = i % (3 * FIR_PAIRS);
+      const long long t = (long long)r - 2 + q;
+      const uint32_t lo = bf16_bits(z_at(A, seg, t, 3 * c0 + 2 * wd));
+      const uint32_t hi = bf16_bits(z_at(A, seg, t, 3 * c0 + 2 * wd + 1));
+      S.zh[q][wd] = lo | (hi << 16);
     }
     __syncthreads();
 
@@ -178,89 +200,110 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
       }
       __syncthreads();
 
-      // ---- K=3 short filter, de-interleave, u = x1*v
-      for (int row = rl; row < n; row += FIR_THREADS / FIR_CG) {
-        float o[3];
+      // ---- K=3 short filter on channel pairs, sliding over 8 consecutive rows
+      const int g0 = rg * FIR_RPT;
+      if (g0 < n) {
+        bf162 w[3][3];
 #pragma unroll
-        for (int q = 0; q < 3; ++q) {
-          const int col = 3 * c + q;
-          const float xm2 = row >= 2 ? __bfloat162float(S.zt[row - 2][col]) : S.zh[row][col];
-          const float xm1 = row >= 1 ? __bfloat162float(S.zt[row - 1][col]) : S.zh[1][col];
-          const float x0 = __bfloat162float(S.zt[row][col]);
-          o[q] = short_tap(xm2, xm1, x0, S.sw[0][col], S.sw[1][col], S.sw[2][col]);
+        for (int c = 0; c < 3; ++c)
+#pragma unroll
+          for (int t = 0; t < 3; ++t) w[c][t] = S.sw[c][t][pp];
+        bf162 h2[3], h1[3];
+        {
+          const uint32_t* a = g0 >= 2 ? &S.zt[g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
+          const uint32_t* b = g0 >= 1 ? &S.zt[g0 - 1][3 * pp] : &S.zh[1][3 * pp];
+          split_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
+          split_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
         }
-        S.ring[ring_idx<RING>((long long)r + row)][c] = bf16r(o[1] * o[2]);
-        S.x2s[row][c] = __float2bfloat16_rn(o[0]);
+        int ri = (r + g0) % RING;
+#pragma unroll
+        for (int i = 0; i < FIR_RPT; ++i) {
+          const int row = g0 + i;
+          if (row < n) {
+            bf162 cur[3], o[3];
+            split_triples(S.zt[row][3 * pp], S.zt[row][3 * pp + 1], S.zt[row][3 * pp + 2],
+                          cur[0], cur[1], cur[2]);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+              o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
+              h2[c] = h1[c];
+              h1[c] = cur[c];
+            }
+            S.ring[ri][pp] = unpack2(__hmul2(o[1], o[2]));
+            S.x2s[row][pp] = o[0];
+          }
+          ri = ri + 1 == RING ? 0 : ri + 1;
+        }
       }
       __syncthreads();
 
       // ---- z history for the next tile (reads zt/zh only; ring untouched)
-      if (tid < 3 * FIR_CG) {
-        const int col = tid;
-        float h0, h1;
+      if (tid < 3 * FIR_PAIRS) {
+        uint32_t h0v, h1v;
         if (n >= 2) {
-          h0 = __bfloat162float(S.zt[n - 2][col]);
-          h1 = __bfloat162float(S.zt[n - 1][col]);
+          h0v = S.zt[n - 2][tid];
+          h1v = S.zt[n - 1][tid];
         } else {
-          h0 = S.zh[1][col];
-          h1 = __bfloat162float(S.zt[0][col]);
+          h0v = S.zh[1][tid];
+          h1v = S.zt[0][tid];
         }
-        S.zh[0][col] = h0;
-        S.zh[1][col] = h1;
+        S.zh[0][tid] = h0v;
+        S.zh[1][tid] = h1v;
       }
 
-      // ---- inner FIR over the ring: thread = (channel c, rows i0..i0+15)
-      const int i0 = rl * FIR_RPT;
+      // ---- inner FIR over the ring: thread = (channel pair, rows i0..i0+7)
+      const int i0 = rg * FIR_RPT;
       if (i0 < n) {
-        float acc[FIR_RPT];
+        float2 acc[FIR_RPT];
 #pragma unroll
-        for (int q = 0; q < FIR_RPT; ++q) acc[q] = 0.0f;
-        const int idx0 = ring_idx<RING>((long long)r + i0 - HIST);
-        float cur[16], nxt[16];
+        for (int q = 0; q < FIR_RPT; ++q) acc[q] = make_float2(0.f, 0.f);
+        int idx0 = (r + i0 - HIST) % RING;
+        idx0 += idx0 < 0 ? RING : 0;
+        float2 cur[8], nxt[8];
 #pragma unroll
-        for (int x = 0; x < 16; ++x) {
+        for (int x = 0; x < 8; ++x) {
           int id = idx0 + x;
           id -= id >= RING ? RING : 0;
-          cur[x] = S.ring[id][c];
+          cur[x] = S.ring[id][pp];
         }
 #pragma unroll
-        for (int kb = 0; kb < K; kb += 16) {
+        for (int kb = 0; kb < K; kb += 8) {
 #pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            if (kb + 16 + x < HIST + FIR_RPT) {
-              int id = idx0 + kb + 16 + x;
+          for (int x = 0; x < 8; ++x) {
+            if (kb + 8 + x < HIST + FIR_RPT) {
+              int id = idx0 + kb + 8 + x;
               id -= id >= RING ? RING : 0;
-              nxt[x] = S.ring[id][c];
+              nxt[x] = S.ring[id][pp];
             }
           }
 #pragma unroll
-          for (int kk = 0; kk < 16; ++kk) {
+          for (int kk = 0; kk < 8; ++kk) {
             if (kb + kk < K) {
-              const float w = __bfloat162float(S.wsm[kb + kk][c]);
+              const float2 wv = unpack2(S.wsm[kb + kk][pp]);
 #pragma unroll
               for (int q = 0; q < FIR_RPT; ++q) {
-                const float uv = (q + kk < 16) ? cur[q + kk] : nxt[q + kk - 16];
-                acc[q] = fmaf(w, uv, acc[q]);
+                const float2 uv = (q + kk < 8) ? cur[q + kk] : nxt[q + kk - 8];
+                acc[q] = ffma2(wv, uv, acc[q]);
               }
             }
           }
 #pragma unroll
-          for (int x = 0; x < 16; ++x) cur[x] = nxt[x];
+          for (int x = 0; x < 8; ++x) cur[x] = nxt[x];
         }
-        const float d = S.dsm[c];
         const bool has_d = Dg != nullptr;
+        const bf162 d2 = S.dsm[pp];
+        bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + i0) * A.ldo + c0) + pp;
+        const long long ld2 = A.ldo / 2;
 #pragma unroll
         for (int q = 0; q < FIR_RPT; ++q) {
           if (i0 + q < n) {
-            float y = bf16r(acc[q]);
+            bf162 y = pack2_rn(acc[q]);
             if (has_d) {
               int id = idx0 + q + HIST;
               id -= id >= RING ? RING : 0;
-              const float u = S.ring[id][c];
-              y = bf16r(y + bf16r(d * u));
+              y = __hadd2(y, __hmul2(d2, pack2_rn(S.ring[id][pp])));
             }
-            const float g = bf16r(__bfloat162float(S.x2s[i0 + q][c]) * y);
-            out[(long long)(r + i0 + q) * A.ldo + c0 + c] = __float2bfloat16_rn(g);
+            outp[q * ld2] = __hmul2(S.x2s[i0 + q][pp], y);
           }
         }
       }

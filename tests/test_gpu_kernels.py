@@ -116,7 +116,10 @@ def test_hcl_prefill_against_float64_scan():
 
 
 @pytest.mark.parametrize("kind,k", KINDS)
-def test_decode_matches_oracle(kind, k):
+@pytest.mark.parametrize("layout", ["sd", "dim_first"])
+def test_decode_matches_oracle(kind, k, layout):
+    """Ordinary decode; the SD layout takes the vectorised q=1 kernels, the
+    dim-first storage (channel stride != 1) the generic kernel."""
     from evo2_flash_b200 import ops
 
     H, B = 256, 5
@@ -126,7 +129,10 @@ def test_decode_matches_oracle(kind, k):
     slots = [3, 1, 6, 2, 7]
     g = torch.Generator().manual_seed(33)
     w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
-    ds = [s.to(DEV) for s in states]
+    if layout == "sd":
+        ds = [s.to(DEV) for s in states]
+    else:  # same logical tensors, stored dim-first
+        ds = [s.to(DEV).transpose(1, 2).contiguous().transpose(1, 2) for s in states]
     ref_states = [s.clone() for s in states]
     for step in range(3):
         z = (torch.randn(B, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
@@ -228,7 +234,8 @@ def test_quant_e4m3_exact():
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
-                                   (4096, 12288, 4096)])
+                                   (4096, 12288, 4096), (128, 12288, 4096), (1024, 4096, 4096),
+                                   (7, 4096, 256)])
 def test_gemm_e4m3(M, N, K):
     from evo2_flash_b200 import ops
 
@@ -245,7 +252,8 @@ def test_gemm_e4m3(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 512), (1000, 776, 192),
-                                   (4096, 4096, 4096)])
+                                   (4096, 4096, 4096), (128, 4096, 4096), (256, 4096, 4096),
+                                   (5, 4104, 128)])
 def test_gemm_bf16_bias(M, N, K):
     from evo2_flash_b200 import ops
 
