@@ -94,6 +94,30 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return c;
 }
 
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long ra, rb, rc;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rc) : "l"(ra), "l"(rb));
+  float2 c;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(c.x), "=f"(c.y) : "l"(rc));
+  return c;
+}
+
+// modal_readout16 on mode pairs (s2[i] = modes 2i, 2i+1): the same halving
+// tree, two modes per instruction.
+__device__ __forceinline__ float modal_readout16_x2(const float2* s2, const float2* r2) {
+  float2 p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmul2(s2[i], r2[i]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = fadd2(p[i], p[i + 4]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) p[i] = fadd2(p[i], p[i + 2]);
+  p[0] = fadd2(p[0], p[1]);
+  return add_rn(p[0].x, p[0].y);
+}
+
 // c + a * b, elementwise on two fp32 lanes, one rounding each (fmaf per lane).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   unsigned long long ra, rb, rc, rd;

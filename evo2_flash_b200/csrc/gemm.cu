@@ -4,13 +4,17 @@
 //   out_proj: out(M,N) bf16 =  A bf16 . B bf16^T + bias          (kind::f16)
 // Both operands K-major (activations (M,K) row-major, nn.Linear weights (N,K)).
 //
-// One CTA computes a 128x256 tile with an fp32 accumulator in tensor memory:
+// Persistent kernel, one CTA per SM, walking 128 x BN output tiles (N fastest)
+// with two fp32 accumulators in tensor memory so that a tile's epilogue overlaps
+// the next tile's main loop:
 //   warp 0     TMA producer: 128-byte-wide K slabs of A and B, SWIZZLE_128B,
-//              into a 4-stage shared-memory ring (no multicast)
+//              into a multi-stage shared-memory ring (no multicast)
 //   warp 1     TMEM allocation + single-thread tcgen05.mma issue; each stage is
-//              released by tcgen05.commit onto its "empty" mbarrier
+//              released by tcgen05.commit onto its "empty" mbarrier, each
+//              finished accumulator by a commit onto its "acc_full" mbarrier
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, scale / bias, bf16,
-//              16-byte global stores
+//              16-byte global stores; the accumulator is handed back ("acc_empty")
+//              as soon as its last column is in registers
 // Every mbarrier wait is bounded by a globaltimer budget; on expiry the kernel
 // records the event in a device counter and runs to completion (TMEM freed).
 #include <cuda.h>
@@ -35,7 +39,7 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
 };
 
 template <int BN>
@@ -44,7 +48,8 @@ struct __align__(1024) Smem {
   uint8_t b[Cfg<BN>::STAGES][Cfg<BN>::B_BYTES];
   uint64_t full[Cfg<BN>::STAGES];
   uint64_t empty[Cfg<BN>::STAGES];
-  uint64_t tmem_full;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint32_t tmem_base;
 };
 
@@ -87,6 +92,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
       return false;
     }
   }
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
                                             int x, int y) {
@@ -166,20 +174,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   Smem<BN>& S = *reinterpret_cast<Smem<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // N is the fastest grid dimension: CTAs resident together share one A row
-  // panel, and the whole weight (<= 50 MB at the 7B shape) stays in L2 while the
-  // activations stream through once.
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
   constexpr int ELEM = FP8 ? 1 : 2;
   constexpr int KE = BKB / ELEM;  // K elements per stage
   const int kblocks = K / KE;
+  // Tiles in N-fastest order: CTAs resident together share A row panels, and the
+  // whole weight (<= 50 MB at the 7B shape) stays in L2 while the activations
+  // stream through once.
+  const int n_tiles = (N + BN - 1) / BN;
+  const int total = n_tiles * ((M + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&S.full[s], 1);
       mbar_init(&S.empty[s], 1);
     }
-    mbar_init(&S.tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.acc_full[b], 1);
+      mbar_init(&S.acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
@@ -198,77 +210,97 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&S.empty[s], ph ^ 1)) break;
-        mbar_expect_tx(&S.full[s], STAGE_BYTES);
-        tma_load_2d(&tmA, &S.full[s], S.a[s], kb * KE, m0);
-        tma_load_2d(&tmB, &S.full[s], S.b[s], kb * KE, n0);
-        issued = kb + 1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(&S.full[s], STAGE_BYTES);
+          tma_load_2d(&tmA, &S.full[s], S.a[s], kb * KE, m0);
+          tma_load_2d(&tmB, &S.full[s], S.b[s], kb * KE, n0);
+        }
       }
       // Drain: every issued copy has landed before the CTA can exit.
-      for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
-        mbar_wait(&S.full[kb % STAGES], (kb / STAGES) & 1);
+      for (uint32_t i = it > (uint32_t)STAGES ? it - STAGES : 0; i < it; ++i)
+        mbar_wait(&S.full[i % STAGES], (i / STAGES) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t ID = idesc<FP8, BN>();
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&S.full[s], ph)) break;
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++ti) {
+        const int b = ti & 1;
+        if (!mbar_wait(&S.acc_empty[b], ((ti >> 1) & 1) ^ 1)) ok = false;
         fence_after();
+        const uint32_t d = tmem + uint32_t(b * BN);
+        for (int kb = 0; kb < kblocks && ok; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&S.full[s], (it / STAGES) & 1)) { ok = false; break; }
+          fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BKB / 32; ++kk) {
-          const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
-          const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
-          mma<FP8>(tmem, ad, bd, ID, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BKB / 32; ++kk) {
+            const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
+            const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
+            mma<FP8>(d, ad, bd, ID, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&S.empty[s]);
         }
-        mma_commit(&S.empty[s]);
+        mma_commit(&S.acc_full[b]);
       }
-      mma_commit(&S.tmem_full);
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool ok = mbar_wait(&S.tmem_full, 0);
-    fence_after();
-    const int row = m0 + 32 * q + lane;
     float scale_a = 1.0f, scale_b = 1.0f;
     if constexpr (FP8) {
       scale_a = __ldg(sa);
       scale_b = __ldg(sb);
     }
+    uint32_t ti = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+      const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+      const int b = ti & 1;
+      const bool ok = mbar_wait(&S.acc_full[b], (ti >> 1) & 1);
+      if (!ok) break;  // the MMA warp gave up: stop rather than time out per tile
+      fence_after();
+      const int row = m0 + 32 * q + lane;
 #pragma unroll 1
-    for (int cb = 0; cb < BN / 32; ++cb) {
-      uint32_t r[32];
-      tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r);
-      const int col0 = n0 + cb * 32;
-      if (!ok || row >= M || col0 >= N) continue;
-      bf16* dst = out + (long long)row * ldo + col0;
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        if (col0 + 8 * v >= N) break;
-        uint4 pk;
-        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float x0 = __uint_as_float(r[8 * v + 2 * e]);
-          float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
-          if constexpr (FP8) {
-            x0 = (x0 * scale_a) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
-            x1 = (x1 * scale_a) * scale_b;
-          } else {
-            if (bias != nullptr) {
-              x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
-              x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
-            }
-          }
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-          pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
+      for (int cb = 0; cb < BN / 32; ++cb) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(b * BN + cb * 32), r);
+        if (cb == BN / 32 - 1) {  // accumulator fully read: hand it back to the MMA warp
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.acc_empty[b]);
         }
-        *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
+        const int col0 = n0 + cb * 32;
+        if (row >= M || col0 >= N) continue;
+        bf16* dst = out + (long long)row * ldo + col0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          if (col0 + 8 * v >= N) break;
+          uint4 pk;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float x0 = __uint_as_float(r[8 * v + 2 * e]);
+            float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
+            if constexpr (FP8) {
+              x0 = (x0 * scale_a) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+              x1 = (x1 * scale_a) * scale_b;
+            } else {
+              if (bias != nullptr) {
+                x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
+                x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
+              }
+            }
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+            pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
+        }
       }
     }
   }
@@ -330,7 +362,15 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
       return check_launch("cudaFuncSetAttribute(gemm)");
     attr = true;
   }
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+  }
+  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  dim3 grid((unsigned)(tiles < sms ? tiles : sms));
   gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
                                                     K, sa, sb, static_cast<const bf16*>(bias));
   return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");

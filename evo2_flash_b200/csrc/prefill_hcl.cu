@@ -87,17 +87,12 @@ __device__ __forceinline__ bool chunk_ctx(const hyena_prefill_args& A, const int
   return true;
 }
 
-// Stages z rows [t0, t0+n) x (3*HCL_CG) columns into shared memory.
-__device__ __forceinline__ void stage_rows(const hyena_prefill_args& A, bf16 (*zt)[3 * HCL_CG],
-                                           int t0, int n, int c0) {
-  const bf16* z = static_cast<const bf16*>(A.z);
-  constexpr int VPR = 3 * HCL_CG * 2 / 16;
-  for (int i = threadIdx.x; i < n * VPR; i += HCL_CG) {
-    const int row = i / VPR, v = i % VPR;
-    *(reinterpret_cast<uint4*>(&zt[row][0]) + v) =
-        __ldg(reinterpret_cast<const uint4*>(z + (long long)(t0 + row) * A.ldz + 3 * c0) + v);
-  }
-}
+struct HclTile {
+  uint32_t zt[HCL_TILE][3 * HCL_CG / 2];  // z rows, raw bf16x2 words
+  uint32_t zh[2][3 * HCL_CG / 2];         // the two z rows before the tile
+  bf162 ug[HCL_TILE][HCL_CG / 2];         // u = bf16(x1*v), channel pairs
+  bf162 x2g[HCL_TILE][HCL_CG / 2];
+};
 
 // z at row t < a (left context of a segment) for column col: cached S0 or zero.
 __device__ __forceinline__ float z_before(const hyena_prefill_args& A, const ChunkCtx& c,
@@ -116,81 +111,135 @@ __device__ __forceinline__ float z_global(const hyena_prefill_args& A, const Chu
   return z_before(A, c, t, col);
 }
 
-// Walks the chunk's rows, calling fn(row, x2, u) in order for this thread's channel.
-template <bool NEED_X2, typename F>
+__device__ __forceinline__ void split_triples_hcl(uint32_t w0, uint32_t w1, uint32_t w2,
+                                                  bf162& x2, bf162& x1, bf162& v) {
+  x2 = as_bf162(__byte_perm(w0, w1, 0x7610));
+  x1 = as_bf162(__byte_perm(w0, w2, 0x5432));
+  v = as_bf162(__byte_perm(w1, w2, 0x7610));
+}
+
+// Walks the chunk's rows in tiles: all threads stage the z rows and run the K=3
+// filter + gate on channel pairs (bf16x2), then fn(row, x2, u) is called in row
+// order with this thread's channel.
+template <typename F>
 __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
                                            const hyena_layer_params& P, const ChunkCtx& c,
-                                           int c0, bf16 (*zt)[3 * HCL_CG], F&& fn) {
+                                           int c0, HclTile& S, F&& fn) {
   const int tid = threadIdx.x;
-  const int h = c0 + tid;
+  constexpr int PAIRS = HCL_CG / 2;
+  constexpr int WORDS = 3 * HCL_CG / 2;
+  const int pp = tid % PAIRS;   // gate: channel pair
+  const int half = tid / PAIRS; // gate: rows [16 half, 16 half + 16) of the tile
   const bf16* sw = static_cast<const bf16*>(P.short_w);
-  float w[3][3];
+  bf162 w[3][3];
+  {
+    const long long h = c0 + 2 * pp;
 #pragma unroll
-  for (int q = 0; q < 3; ++q)
+    for (int col = 0; col < 3; ++col)
 #pragma unroll
-    for (int t = 0; t < 3; ++t) w[q][t] = ldbf(sw + (3 * h + q) * 3 + t);
-  // z history (rows row0-2, row0-1) of the three columns
-  float hm2[3], hm1[3];
-#pragma unroll
-  for (int q = 0; q < 3; ++q) {
-    hm2[q] = z_global(A, c, (long long)c.row0 - 2, 3 * h + q);
-    hm1[q] = z_global(A, c, (long long)c.row0 - 1, 3 * h + q);
+      for (int t = 0; t < 3; ++t)
+        w[col][t] = __halves2bfloat162(sw[(3 * h + col) * 3 + t], sw[(3 * (h + 1) + col) * 3 + t]);
   }
+  for (int i = tid; i < 2 * WORDS; i += HCL_CG) {
+    const int q = i / WORDS, wd = i % WORDS;
+    const long long t = (long long)c.row0 - 2 + q;
+    const uint32_t lo = (uint32_t)__bfloat16_as_ushort(
+        __float2bfloat16_rn(z_global(A, c, t, 3 * c0 + 2 * wd)));
+    const uint32_t hi = (uint32_t)__bfloat16_as_ushort(
+        __float2bfloat16_rn(z_global(A, c, t, 3 * c0 + 2 * wd + 1)));
+    S.zh[q][wd] = lo | (hi << 16);
+  }
+  const bf16* z = static_cast<const bf16*>(A.z);
   for (int t0 = c.row0; t0 < c.row1; t0 += HCL_TILE) {
     const int n = min(HCL_TILE, c.row1 - t0);
-    __syncthreads();
-    stage_rows(A, zt, t0, n, c0);
-    __syncthreads();
-    for (int row = 0; row < n; ++row) {
-      float o[3];
-#pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        if (!NEED_X2 && q == 0) { o[0] = 0.0f; continue; }
-        const float x0 = __bfloat162float(zt[row][3 * tid + q]);
-        o[q] = short_tap(hm2[q], hm1[q], x0, w[q][0], w[q][1], w[q][2]);
-        hm2[q] = hm1[q];
-        hm1[q] = x0;
-      }
-      fn(t0 + row, o[0], bf16r(o[1] * o[2]));
+    constexpr int VPR = WORDS * 4 / 16;
+    for (int i = tid; i < n * VPR; i += HCL_CG) {
+      const int row = i / VPR, v = i % VPR;
+      *(reinterpret_cast<uint4*>(&S.zt[row][0]) + v) =
+          __ldg(reinterpret_cast<const uint4*>(z + (long long)(t0 + row) * A.ldz + 3 * c0) + v);
     }
+    __syncthreads();
+    {
+      const int g0 = half * (HCL_TILE / 2);
+      bf162 h2[3], h1[3];
+      const uint32_t* a = g0 >= 2 ? &S.zt[g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
+      const uint32_t* b = g0 >= 1 ? &S.zt[g0 - 1][3 * pp] : &S.zh[1][3 * pp];
+      split_triples_hcl(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
+      split_triples_hcl(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
+#pragma unroll 4
+      for (int i = 0; i < HCL_TILE / 2; ++i) {
+        const int row = g0 + i;
+        if (row < n) {
+          bf162 cur[3], o[3];
+          split_triples_hcl(S.zt[row][3 * pp], S.zt[row][3 * pp + 1], S.zt[row][3 * pp + 2],
+                            cur[0], cur[1], cur[2]);
+#pragma unroll
+          for (int col = 0; col < 3; ++col) {
+            o[col] = short_tap2(h2[col], h1[col], cur[col], w[col][0], w[col][1], w[col][2]);
+            h2[col] = h1[col];
+            h1[col] = cur[col];
+          }
+          S.ug[row][pp] = __hmul2(o[1], o[2]);
+          S.x2g[row][pp] = o[0];
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < WORDS; i += HCL_CG) {  // z history for the next tile
+      const uint32_t a0 = n >= 2 ? S.zt[n - 2][i] : S.zh[1][i];
+      const uint32_t a1 = S.zt[n - 1][i];
+      S.zh[0][i] = a0;
+      S.zh[1][i] = a1;
+    }
+    const bf16* ug = reinterpret_cast<const bf16*>(&S.ug[0][0]);
+    const bf16* xg = reinterpret_cast<const bf16*>(&S.x2g[0][0]);
+    for (int row = 0; row < n; ++row)
+      fn(t0 + row, ldbf(xg + row * HCL_CG + tid), ldbf(ug + row * HCL_CG + tid));
+    __syncthreads();
   }
 }
 
-__device__ __forceinline__ void load_poles(const hyena_layer_params& P, int h, float* p) {
+__device__ __forceinline__ void load_pole_pairs(const hyena_layer_params& P, int h, float2* p2,
+                                                float scale) {
+  const float* lp = P.log_poles + (long long)h * P.lp_stride_h;
 #pragma unroll
-  for (int s = 0; s < HCL_S; ++s) p[s] = expf(P.log_poles[(long long)h * P.lp_stride_h + s * P.lp_stride_s]);
+  for (int i = 0; i < HCL_S / 2; ++i)
+    p2[i] = make_float2(expf(lp[(2 * i) * P.lp_stride_s] * scale),
+                        expf(lp[(2 * i + 1) * P.lp_stride_s] * scale));
 }
 
 __global__ void __launch_bounds__(HCL_CG)
 hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
-  __shared__ __align__(16) bf16 zt[HCL_TILE][3 * HCL_CG];
+  __shared__ __align__(16) HclTile S;
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
   if (c.k == c.nch - 1) return;  // the final chunk's aggregate is never needed
   const int c0 = blockIdx.y * HCL_CG;
   const int h = c0 + threadIdx.x;
   if (c.init && (c.blk < 0 || c.blk >= A.conv_state.num_blocks)) c.init = false;
-  float p[HCL_S], acc[HCL_S];
-  load_poles(P, h, p);
+  float2 p2[HCL_S / 2], acc[HCL_S / 2];
+  load_pole_pairs(P, h, p2, 1.0f);
 #pragma unroll
-  for (int s = 0; s < HCL_S; ++s) acc[s] = 0.0f;
-  walk_chunk<false>(A, P, c, c0, zt, [&](int, float, float u) {
+  for (int i = 0; i < HCL_S / 2; ++i) acc[i] = make_float2(0.f, 0.f);
+  walk_chunk(A, P, c, c0, S, [&](int, float, float u) {
+    const float2 uu = make_float2(u, u);
 #pragma unroll
-    for (int s = 0; s < HCL_S; ++s) acc[s] = add_rn(mul_rn(acc[s], p[s]), u);
+    for (int i = 0; i < HCL_S / 2; ++i) acc[i] = fadd2(fmul2(acc[i], p2[i]), uu);
   });
   float4* dst = reinterpret_cast<float4*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
 #pragma unroll
-  for (int s = 0; s < HCL_S / 4; ++s)
-    dst[s] = make_float4(acc[4 * s], acc[4 * s + 1], acc[4 * s + 2], acc[4 * s + 3]);
+  for (int i = 0; i < HCL_S / 4; ++i)
+    dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
 }
 
-// One thread per (segment, channel): S_in for every chunk, written over the
-// chunk's aggregate.
+// One thread per (segment, channel, mode): S_in for every chunk, written over
+// the chunk's aggregate.
 __global__ void __launch_bounds__(128)
 hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
   const int j = blockIdx.x;
-  const int h = blockIdx.y * 128 + threadIdx.x;
-  if (h >= P.H) return;
+  const long long idx = (long long)blockIdx.y * 128 + threadIdx.x;  // h * 16 + s
+  if (idx >= (long long)P.H * HCL_S) return;
+  const int h = (int)(idx / HCL_S), s = (int)(idx % HCL_S);
   const int base = __ldg(W.chunk_base + j);
   const int nch = __ldg(W.chunk_base + j + 1) - base;
   if (nch <= 0) return;
@@ -200,38 +249,25 @@ hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWork
     flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
     init = false;
   }
-  float S[HCL_S], pc[HCL_S];
   const float* s2 = static_cast<const float*>(A.inner_state.data);
-#pragma unroll
-  for (int s = 0; s < HCL_S; ++s) {
-    S[s] = init ? s2[blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
-                     (long long)s * A.inner_state.col_stride]
-                : 0.0f;
-    pc[s] = expf(P.log_poles[(long long)h * P.lp_stride_h + s * P.lp_stride_s] * (float)HCL_C);
-  }
+  float S = init ? s2[blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
+                      (long long)s * A.inner_state.col_stride]
+                 : 0.0f;
+  const float pc = expf(P.log_poles[(long long)h * P.lp_stride_h + s * P.lp_stride_s] * (float)HCL_C);
+  float* slot = W.states + (long long)base * P.H * HCL_S + idx;
+  const long long stride = (long long)P.H * HCL_S;
+  float a = nch > 1 ? slot[0] : 0.0f;
   for (int k = 0; k < nch; ++k) {
-    float4* slot = reinterpret_cast<float4*>(W.states + ((long long)(base + k) * P.H + h) * HCL_S);
-    float a[HCL_S];
-    if (k < nch - 1) {
-#pragma unroll
-      for (int s = 0; s < HCL_S / 4; ++s) {
-        const float4 v = slot[s];
-        a[4 * s] = v.x; a[4 * s + 1] = v.y; a[4 * s + 2] = v.z; a[4 * s + 3] = v.w;
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < HCL_S / 4; ++s)
-      slot[s] = make_float4(S[4 * s], S[4 * s + 1], S[4 * s + 2], S[4 * s + 3]);
-    if (k < nch - 1) {
-#pragma unroll
-      for (int s = 0; s < HCL_S; ++s) S[s] = add_rn(mul_rn(pc[s], S[s]), a[s]);
-    }
+    const float next = (k + 1 < nch - 1) ? slot[(k + 1) * stride] : 0.0f;  // prefetch
+    slot[k * stride] = S;
+    if (k < nch - 1) S = add_rn(mul_rn(pc, S), a);
+    a = next;
   }
 }
 
 __global__ void __launch_bounds__(HCL_CG)
 hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
-  __shared__ __align__(16) bf16 zt[HCL_TILE][3 * HCL_CG];
+  __shared__ __align__(16) HclTile S;
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
   const int c0 = blockIdx.y * HCL_CG;
@@ -239,26 +275,30 @@ hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWor
   const bool blk_ok = c.blk >= 0 && c.blk < A.inner_state.num_blocks &&
                       c.blk < A.conv_state.num_blocks;
   if (c.init && !blk_ok) c.init = false;
-  float p[HCL_S], r[HCL_S], s[HCL_S];
-  load_poles(P, h, p);
-#pragma unroll
-  for (int q = 0; q < HCL_S; ++q) r[q] = P.residues[(long long)h * P.res_stride_h + q * P.res_stride_s];
+  float2 p2[HCL_S / 2], r2[HCL_S / 2], s2[HCL_S / 2];
+  load_pole_pairs(P, h, p2, 1.0f);
   {
+    const float* rr = P.residues + (long long)h * P.res_stride_h;
+#pragma unroll
+    for (int i = 0; i < HCL_S / 2; ++i)
+      r2[i] = make_float2(rr[(2 * i) * P.res_stride_s], rr[(2 * i + 1) * P.res_stride_s]);
     const float4* src =
         reinterpret_cast<const float4*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
 #pragma unroll
-    for (int q = 0; q < HCL_S / 4; ++q) {
-      const float4 v = src[q];
-      s[4 * q] = v.x; s[4 * q + 1] = v.y; s[4 * q + 2] = v.z; s[4 * q + 3] = v.w;
+    for (int i = 0; i < HCL_S / 4; ++i) {
+      const float4 v = src[i];
+      s2[2 * i] = make_float2(v.x, v.y);
+      s2[2 * i + 1] = make_float2(v.z, v.w);
     }
   }
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float d = Dg ? ldbf(Dg + h) : 0.0f;
   bf16* out = static_cast<bf16*>(A.out);
-  walk_chunk<true>(A, P, c, c0, zt, [&](int row, float x2, float u) {
+  walk_chunk(A, P, c, c0, S, [&](int row, float x2, float u) {
+    const float2 uu = make_float2(u, u);
 #pragma unroll
-    for (int q = 0; q < HCL_S; ++q) s[q] = add_rn(mul_rn(s[q], p[q]), u);
-    float y = bf16r(modal_readout16(s, r));
+    for (int i = 0; i < HCL_S / 2; ++i) s2[i] = fadd2(fmul2(s2[i], p2[i]), uu);
+    float y = bf16r(modal_readout16_x2(s2, r2));
     if (Dg) y = bf16r(y + bf16r(u * d));
     out[(long long)row * A.ldo + h] = __float2bfloat16_rn(bf16r(y * x2));
   });
@@ -267,11 +307,13 @@ hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWor
       if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
       return;
     }
-    float* s2 = static_cast<float*>(A.inner_state.data);
+    float* st = static_cast<float*>(A.inner_state.data);
 #pragma unroll
-    for (int q = 0; q < HCL_S; ++q)
-      s2[c.blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
-         (long long)q * A.inner_state.col_stride] = s[q];
+    for (int i = 0; i < HCL_S / 2; ++i) {
+      const long long b = c.blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride;
+      st[b + (long long)(2 * i) * A.inner_state.col_stride] = s2[i].x;
+      st[b + (long long)(2 * i + 1) * A.inner_state.col_stride] = s2[i].y;
+    }
   }
 }
 
@@ -294,7 +336,7 @@ int hcl_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
   if (rc) return rc;
   hcl_aggregate_kernel<<<dim3(max_chunks, groups), HCL_CG, 0, st>>>(P, A, W);
   if ((rc = check_launch("hcl_aggregate_kernel"))) return rc;
-  hcl_carry_kernel<<<dim3(A.num_segments, (P.H + 127) / 128), 128, 0, st>>>(P, A, W);
+  hcl_carry_kernel<<<dim3(A.num_segments, (P.H * HCL_S + 127) / 128), 128, 0, st>>>(P, A, W);
   if ((rc = check_launch("hcl_carry_kernel"))) return rc;
   hcl_output_kernel<<<dim3(max_chunks, groups), HCL_CG, 0, st>>>(P, A, W);
   if ((rc = check_launch("hcl_output_kernel"))) return rc;
