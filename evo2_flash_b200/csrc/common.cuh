@@ -130,14 +130,55 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// Two fp32 lanes held in one 64-bit register (lo = first element).  Keeping
+// packed values in this type end to end lets fma/mul/add.f32x2 run without
+// register-pair shuffles.
+typedef unsigned long long f2;
+
+__device__ __forceinline__ f2 f2_make(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(f2 v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// bf16x2 word -> two fp32 lanes (exact)
+__device__ __forceinline__ f2 f2_from_bf162(bf162 v) {
+  const uint32_t w = as_u32(v);
+  return (f2)(w << 16) | ((f2)(w & 0xffff0000u) << 32);
+}
+// two fp32 lanes -> bf16x2, round to nearest even
+__device__ __forceinline__ bf162 bf162_from_f2(f2 v) {
+  const float2 x = f2_split(v);
+  return __floats2bfloat162_rn(x.x, x.y);
+}
+
 // short_tap on a channel pair: products rounded to bf16 (bf16x2 multiply),
 // summed oldest first in fp32, result rounded to bf16.
 __device__ __forceinline__ bf162 short_tap2(bf162 c0, bf162 c1, bf162 x, bf162 w0, bf162 w1,
                                             bf162 w2) {
-  const float2 p0 = unpack2(__hmul2(c0, w0));
-  const float2 p1 = unpack2(__hmul2(c1, w1));
-  const float2 p2 = unpack2(__hmul2(x, w2));
-  return pack2_rn(fadd2(fadd2(p0, p1), p2));
+  const f2 p0 = f2_from_bf162(__hmul2(c0, w0));
+  const f2 p1 = f2_from_bf162(__hmul2(c1, w1));
+  const f2 p2 = f2_from_bf162(__hmul2(x, w2));
+  return bf162_from_f2(f2_add(f2_add(p0, p1), p2));
 }
 
 // Largest j with qsl[j] <= row, for a non-decreasing qsl[0..n].

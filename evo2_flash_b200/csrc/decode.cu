@@ -257,7 +257,12 @@ __device__ __forceinline__ void short_gate_q1(const hyena_layer_params& P,
   bf16* s0 = static_cast<bf16*>(A.conv_state.data);
   const bf16* c0p = s0 + cin * A.conv_state.block_stride + 3 * h;
   const bf16* c1p = c0p + A.conv_state.col_stride;
-  const bf16* sw = static_cast<const bf16*>(P.short_w) + 9 * h;
+  // short taps of the C channels: 9C contiguous bf16, 8-byte aligned for C % 4 == 0
+  const uint2* swv = reinterpret_cast<const uint2*>(static_cast<const bf16*>(P.short_w) + 9 * h);
+  uint2 swr[9 * C / 4];
+#pragma unroll
+  for (int i = 0; i < 9 * C / 4; ++i) swr[i] = __ldg(swv + i);
+  const bf16* sw = reinterpret_cast<const bf16*>(swr);
   float zx[3 * C], w0[3 * C], w1[3 * C];
 #pragma unroll
   for (int i = 0; i < 3 * C; i += 4) {
@@ -273,7 +278,8 @@ __device__ __forceinline__ void short_gate_q1(const hyena_layer_params& P,
   float o[3 * C];
 #pragma unroll
   for (int i = 0; i < 3 * C; ++i)
-    o[i] = short_tap(w0[i], w1[i], zx[i], ldbf(sw + 3 * i), ldbf(sw + 3 * i + 1), ldbf(sw + 3 * i + 2));
+    o[i] = short_tap(w0[i], w1[i], zx[i], __bfloat162float(sw[3 * i]),
+                     __bfloat162float(sw[3 * i + 1]), __bfloat162float(sw[3 * i + 2]));
   if (write_conv) {
     bf16* d0 = s0 + cout * A.conv_state.block_stride + 3 * h;
     bf16* d1 = d0 + A.conv_state.col_stride;
@@ -296,7 +302,7 @@ template <int K>
 __global__ void __launch_bounds__(FAST_THREADS)
 decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   constexpr int HIST = K - 1;
-  constexpr int U = 16;  // taps in flight
+  constexpr int U = 8;  // taps in flight
   const int r = blockIdx.x;
   const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
   if (h >= P.H) return;
@@ -330,22 +336,24 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 #pragma unroll 1
   for (int k0 = 0; k0 < HIST; k0 += U) {
     float4 sv[U];
-    float wv[U][4];
+    uint2 wr[U];
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       if (k0 + t < HIST) {
         sv[t] = src_ok ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + t) * cs)
                        : make_float4(0.f, 0.f, 0.f, 0.f);
-        load_bf16x4(w + (long long)(k0 + t) * wk, wv[t]);
+        wr[t] = __ldg(reinterpret_cast<const uint2*>(w + (long long)(k0 + t) * wk));
       }
     }
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       if (k0 + t < HIST) {
-        acc[0] = fmaf(wv[t][0], sv[t].x, acc[0]);
-        acc[1] = fmaf(wv[t][1], sv[t].y, acc[1]);
-        acc[2] = fmaf(wv[t][2], sv[t].z, acc[2]);
-        acc[3] = fmaf(wv[t][3], sv[t].w, acc[3]);
+        const float2 wa = __bfloat1622float2(as_bf162(wr[t].x));
+        const float2 wb = __bfloat1622float2(as_bf162(wr[t].y));
+        acc[0] = fmaf(wa.x, sv[t].x, acc[0]);
+        acc[1] = fmaf(wa.y, sv[t].y, acc[1]);
+        acc[2] = fmaf(wb.x, sv[t].z, acc[2]);
+        acc[3] = fmaf(wb.y, sv[t].w, acc[3]);
         if (dok && k0 + t >= 1) *reinterpret_cast<float4*>(dp + (long long)(k0 + t - 1) * cs) = sv[t];
       }
     }
@@ -370,71 +378,68 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 
 __global__ void __launch_bounds__(FAST_THREADS)
 decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  __shared__ float u_s[FAST_THREADS], x2_s[FAST_THREADS];
   const int r = blockIdx.x;
-  const int h = blockIdx.y * FAST_THREADS + threadIdx.x;
-  if (h >= P.H) return;
+  const int hb0 = blockIdx.y * FAST_THREADS;
+  const int h = hb0 + threadIdx.x;
   const long long cin = __ldg(A.conv_in_block + r);
   const long long cout = __ldg(A.conv_out_block + r);
-  bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo + h;
+  bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo;
   if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
     if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
       flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-    *out = __float2bfloat16_rn(0.0f);
+    if (h < P.H) out[h] = __float2bfloat16_rn(0.0f);
     return;
   }
-  const bool write_conv = block_ok(cout, A.conv_state) &&
-                          !(A.skip_null_writes && cout == A.null_block);
-  // one channel: scalar short filter
-  const bf16* z = static_cast<const bf16*>(A.z) + (long long)r * A.ldz + 3 * h;
-  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
-  const bf16* sw = static_cast<const bf16*>(P.short_w) + 9 * h;
-  float o[3];
-#pragma unroll
-  for (int q = 0; q < 3; ++q) {
-    const long long base = cin * A.conv_state.block_stride + 3 * h + q;
-    const float c0 = ldbf(s0 + base), c1 = ldbf(s0 + base + A.conv_state.col_stride);
-    const float x = ldbf(z + q);
-    o[q] = short_tap(c0, c1, x, ldbf(sw + 3 * q), ldbf(sw + 3 * q + 1), ldbf(sw + 3 * q + 2));
-    if (write_conv) {
-      const long long ob = cout * A.conv_state.block_stride + 3 * h + q;
-      s0[ob] = __float2bfloat16_rn(c1);
-      s0[ob + A.conv_state.col_stride] = __float2bfloat16_rn(x);
-    }
-  }
-  const float u = bf16r(o[1] * o[2]);
   const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
   const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
   const bool src_ok = block_ok(src, A.inner_state);
   const bool dok = block_ok(dst, A.inner_state) && !(A.skip_null_writes && dst == A.null_block);
   if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+  // state and parameters first: 16-byte loads in flight while the gate runs
   float* st = static_cast<float*>(A.inner_state.data);
-  const float4* sp = reinterpret_cast<const float4*>(
-      st + (src_ok ? src : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
-  float4* dp = reinterpret_cast<float4*>(
-      st + (dok ? dst : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
   float s[16], pl[16], rs[16];
+  if (h < P.H) {
+    const float4* sp = reinterpret_cast<const float4*>(
+        st + (src_ok ? src : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
+    const float4* lp = reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h);
+    const float4* rr = reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 v = src_ok ? sp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-    s[4 * q] = v.x; s[4 * q + 1] = v.y; s[4 * q + 2] = v.z; s[4 * q + 3] = v.w;
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = src_ok ? sp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 a = __ldg(lp + q), b = __ldg(rr + q);
+      s[4 * q] = v.x; s[4 * q + 1] = v.y; s[4 * q + 2] = v.z; s[4 * q + 3] = v.w;
+      pl[4 * q] = a.x; pl[4 * q + 1] = a.y; pl[4 * q + 2] = a.z; pl[4 * q + 3] = a.w;
+      rs[4 * q] = b.x; rs[4 * q + 1] = b.y; rs[4 * q + 2] = b.z; rs[4 * q + 3] = b.w;
+    }
   }
-  const float* lp = P.log_poles + (long long)h * P.lp_stride_h;
-  const float* rr = P.residues + (long long)h * P.res_stride_h;
+  // gate: 4 channels per thread on the first FAST_THREADS/4 threads
+  if (threadIdx.x < FAST_THREADS / 4 && hb0 + 4 * threadIdx.x < P.H) {
+    const bool write_conv = block_ok(cout, A.conv_state) &&
+                            !(A.skip_null_writes && cout == A.null_block);
+    float x2[4], u[4];
+    short_gate_q1<4>(P, A, r, hb0 + 4 * threadIdx.x, cin, cout, write_conv, x2, u);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) {
-    pl[q] = expf(lp[q * P.lp_stride_s]);
-    rs[q] = rr[q * P.res_stride_s];
+    for (int c = 0; c < 4; ++c) {
+      u_s[4 * threadIdx.x + c] = u[c];
+      x2_s[4 * threadIdx.x + c] = x2[c];
+    }
   }
+  __syncthreads();
+  if (h >= P.H) return;
+  const float u = u_s[threadIdx.x];
 #pragma unroll
-  for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u);
+  for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], expf(pl[q])), u);
   if (dok) {
+    float4* dp = reinterpret_cast<float4*>(st + dst * A.inner_state.block_stride +
+                                           (long long)h * A.inner_state.dim_stride);
 #pragma unroll
     for (int q = 0; q < 4; ++q) dp[q] = make_float4(s[4 * q], s[4 * q + 1], s[4 * q + 2], s[4 * q + 3]);
   }
   float y = bf16r(modal_readout16(s, rs));
   const bf16* Dg = static_cast<const bf16*>(P.D);
   if (Dg) y = bf16r(y + bf16r(ldbf(Dg + h) * u));
-  *out = __float2bfloat16_rn(bf16r(o[0] * y));
+  out[h] = __float2bfloat16_rn(bf16r(x2_s[threadIdx.x] * y));
 }
 
 static bool aligned_elems(const void* p, int64_t stride_elems, int elem_bytes, int vec_bytes) {
@@ -448,6 +453,7 @@ static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A
   if (A.q != 1 || A.token_start != nullptr || A.accepted != nullptr) return false;
   if (A.conv_state.cols != 2 || A.conv_state.dim_stride != 1) return false;
   if (!aligned_elems(A.z, A.ldz, 2, 8) || !aligned_elems(A.out, A.ldo, 2, 8)) return false;
+  if (!aligned_elems(P.short_w, 0, 2, 8)) return false;
   if (!aligned_elems(A.conv_state.data, A.conv_state.block_stride, 2, 8) ||
       (A.conv_state.col_stride * 2) % 8 != 0)
     return false;
@@ -459,7 +465,9 @@ static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A
            P.H % 4 == 0;
   }
   return s.col_stride == 1 && aligned_elems(s.data, s.block_stride, 4, 16) &&
-         (s.dim_stride * 4) % 16 == 0;
+         (s.dim_stride * 4) % 16 == 0 && P.lp_stride_s == 1 && P.res_stride_s == 1 &&
+         aligned_elems(P.log_poles, P.lp_stride_h, 4, 16) &&
+         aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % 4 == 0;
 }
 
 int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaStream_t st) {

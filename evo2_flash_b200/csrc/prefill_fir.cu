@@ -21,27 +21,23 @@ namespace hb {
 
 constexpr int FIR_CG = 64;       // channels per CTA
 constexpr int FIR_PAIRS = FIR_CG / 2;
-constexpr int FIR_BT = 64;       // rows per tile
-constexpr int FIR_THREADS = 256;
+constexpr int FIR_BT = 128;      // rows per tile
+constexpr int FIR_THREADS = 512;
 constexpr int FIR_RPT = 8;       // rows per thread in the gate and tap phases
+constexpr int FIR_RING = 256;    // u ring rows (power of two >= K-1 + FIR_BT)
+constexpr int FIR_WORDS = 3 * FIR_PAIRS;  // bf16x2 words of z per row per CTA
 constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
-
-template <int K>
-struct FirCfg {
-  static constexpr int HIST = K - 1;
-  static constexpr int RING = ((HIST + FIR_BT + 15) / 16) * 16;
-};
 
 // Thread (pair p = tid % 32, row group g = tid / 32) owns channels c0+2p, c0+2p+1
 // and tile rows 8g .. 8g+7 in both the gate and the tap phases.
 template <int K>
 struct FirShared {
-  float2 ring[FirCfg<K>::RING][FIR_PAIRS];  // u by row (mod RING), fp32 pairs
-  uint32_t zt[FIR_BT][3 * FIR_PAIRS];       // z tile, raw bf16x2 words
-  bf162 x2s[FIR_BT][FIR_PAIRS];             // x2 of the tile
-  bf162 wsm[K][FIR_PAIRS];                  // inner taps, [k][pair]
-  uint32_t zh[2][3 * FIR_PAIRS];            // z rows (r-2, r-1) before the tile
-  bf162 sw[3][3][FIR_PAIRS];                // short taps [column x2/x1/v][tap][pair]
+  f2 ring[FIR_RING][FIR_PAIRS];          // u by row (mod FIR_RING), fp32 pairs
+  uint32_t zt[2][FIR_BT][FIR_WORDS];     // z tiles (double buffered), raw bf16x2 words
+  bf162 x2s[FIR_BT][FIR_PAIRS];          // x2 of the tile
+  f2 wsm[K][FIR_PAIRS];                  // inner taps as fp32 pairs, [k][pair]
+  uint32_t zh[2][FIR_WORDS];             // z rows (r-2, r-1) before the tile
+  bf162 sw[3][3][FIR_PAIRS];             // short taps [column x2/x1/v][tap][pair]
   bf162 dsm[FIR_PAIRS];
 };
 
@@ -102,11 +98,53 @@ __device__ __forceinline__ void split_triples(uint32_t w0, uint32_t w1, uint32_t
   v = as_bf162(__byte_perm(w1, w2, 0x7610));
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Tiles walk the CTA's rows [r0, r1) and never straddle a segment boundary.
+struct TileIt {
+  int r, n, j;
+};
+
+__device__ __forceinline__ TileIt tile_at(const hyena_prefill_args& A, int r, int r1, int j) {
+  const int nseg = A.num_segments;
+  while (j < nseg && __ldg(A.query_start_loc + j + 1) <= r) ++j;
+  TileIt t;
+  t.r = r;
+  t.j = j;
+  t.n = (j < nseg && r < r1) ? min(FIR_BT, min(__ldg(A.query_start_loc + j + 1), r1) - r) : 0;
+  return t;
+}
+
 template <int K>
-__global__ void __launch_bounds__(FIR_THREADS, 2)
+__device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefill_args& A,
+                                              const TileIt& t, int buf, int c0) {
+  const bf16* z = static_cast<const bf16*>(A.z);
+  constexpr int VPR = FIR_WORDS * 4 / 16;  // 16-byte vectors per row
+  for (int i = threadIdx.x; i < t.n * VPR; i += FIR_THREADS) {
+    const int row = i / VPR, v = i % VPR;
+    cp_async16(reinterpret_cast<uint4*>(&S.zt[buf][row][0]) + v,
+               reinterpret_cast<const uint4*>(z + (long long)(t.r + row) * A.ldz + 3 * c0) + v);
+  }
+  cp_async_commit();
+}
+
+template <int K>
+__global__ void __launch_bounds__(FIR_THREADS, 1)
 fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
-  constexpr int RING = FirCfg<K>::RING;
   constexpr int HIST = K - 1;
+  static_assert(HIST + FIR_BT <= FIR_RING, "ring too small");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FirShared<K>& S = *reinterpret_cast<FirShared<K>*>(smem_raw);
 
@@ -119,18 +157,22 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   const int r1 = min(T_end, r0 + rows_per_cta);
   if (r0 >= r1) return;
 
-  const bf16* z = static_cast<const bf16*>(A.z);
   bf16* out = static_cast<bf16*>(A.out);
   const bf16* iw = static_cast<const bf16*>(P.inner_w);
   const bf16* swg = static_cast<const bf16*>(P.short_w);
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float* s1 = static_cast<const float*>(A.inner_state.data);
 
+  TileIt t = tile_at(A, r0, r1, find_segment(qsl, nseg, r0));
+  int buf = 0;
+  if (t.n > 0) prefetch_tile(S, A, t, buf, c0);
+
   for (int i = tid; i < K * FIR_PAIRS; i += FIR_THREADS) {
     const int k = i / FIR_PAIRS, pp = i % FIR_PAIRS;
     const long long h = c0 + 2 * pp;
-    S.wsm[k][pp] = __halves2bfloat162(iw[h * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k],
-                                      iw[(h + 1) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]);
+    S.wsm[k][pp] = f2_make(
+        __bfloat162float(iw[h * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]),
+        __bfloat162float(iw[(h + 1) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]));
   }
   for (int i = tid; i < 9 * FIR_PAIRS; i += FIR_THREADS) {
     const int col = i / (3 * FIR_PAIRS), tap = (i / FIR_PAIRS) % 3, pp = i % FIR_PAIRS;
@@ -141,176 +183,146 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   if (tid < FIR_PAIRS)
     S.dsm[tid] = Dg ? __halves2bfloat162(Dg[c0 + 2 * tid], Dg[c0 + 2 * tid + 1])
                     : __floats2bfloat162_rn(0.f, 0.f);
-  __syncthreads();
 
   const int pp = tid % FIR_PAIRS;  // channel pair
-  const int rg = tid / FIR_PAIRS;  // row group 0..7
+  const int rg = tid / FIR_PAIRS;  // row group 0..15
   float* ring_f = reinterpret_cast<float*>(&S.ring[0][0]);
+  int cur_seg = -1;
 
-  int r = r0;
-  int j = find_segment(qsl, nseg, r);
-  while (r < r1) {
-    while (j < nseg && __ldg(qsl + j + 1) <= r) ++j;
-    if (j >= nseg) break;
-    SegCtx seg = load_segment(A, j);
-    if (seg.a > r) { r = seg.a; continue; }  // defensive: qsl must tile the rows
-    if (seg.init && (seg.blk < 0 || seg.blk >= A.inner_state.num_blocks ||
-                     seg.blk >= A.conv_state.num_blocks)) {
-      if (tid == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-      seg.init = false;
-    }
+  while (t.n > 0) {
+    const TileIt nt = tile_at(A, t.r + t.n, r1, t.j);
+    if (nt.n > 0) prefetch_tile(S, A, nt, buf ^ 1, c0);
 
-    // ---- history for row r: ring rows [r-HIST, r) and z rows r-2, r-1
-    for (int i = tid; i < HIST * FIR_CG; i += FIR_THREADS) {
-      const int m = i / FIR_CG + 1, cc = i % FIR_CG;
-      const long long t = (long long)r - m;
-      float val;
-      if (t >= seg.a) {
-        val = u_at(A, P, seg, t, c0 + cc);
-      } else if (seg.init && seg.a - t <= HIST) {
-        const long long col = HIST - (seg.a - t);
-        val = s1[seg.blk * A.inner_state.block_stride + col * A.inner_state.col_stride +
-                 (long long)(c0 + cc) * A.inner_state.dim_stride];
-      } else {
-        val = 0.0f;
+    if (t.j != cur_seg) {
+      // ---- new segment (or the CTA's first rows): history rows [r-HIST, r) and z rows r-2, r-1
+      cur_seg = t.j;
+      SegCtx seg = load_segment(A, t.j);
+      if (seg.init && (seg.blk < 0 || seg.blk >= A.inner_state.num_blocks ||
+                       seg.blk >= A.conv_state.num_blocks)) {
+        if (tid == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+        seg.init = false;
       }
-      int ri = (int)(t % RING);
-      ri += ri < 0 ? RING : 0;
-      ring_f[ri * FIR_CG + cc] = val;
+      __syncthreads();  // previous tile's readers of ring / zh are done
+      for (int i = tid; i < HIST * FIR_CG; i += FIR_THREADS) {
+        const int m = i / FIR_CG + 1, cc = i % FIR_CG;
+        const long long tr = (long long)t.r - m;
+        float val;
+        if (tr >= seg.a) {
+          val = u_at(A, P, seg, tr, c0 + cc);
+        } else if (seg.init && seg.a - tr <= HIST) {
+          const long long col = HIST - (seg.a - tr);
+          val = s1[seg.blk * A.inner_state.block_stride + col * A.inner_state.col_stride +
+                   (long long)(c0 + cc) * A.inner_state.dim_stride];
+        } else {
+          val = 0.0f;
+        }
+        ring_f[(int)(tr & (FIR_RING - 1)) * FIR_CG + cc] = val;
+      }
+      for (int i = tid; i < 2 * FIR_WORDS; i += FIR_THREADS) {
+        const int q = i / FIR_WORDS, wd = i % FIR_WORDS;
+        const long long tr = (long long)t.r - 2 + q;
+        const uint32_t lo = bf16_bits(z_at(A, seg, tr, 3 * c0 + 2 * wd));
+        const uint32_t hi = bf16_bits(z_at(A, seg, tr, 3 * c0 + 2 * wd + 1));
+        S.zh[q][wd] = lo | (hi << 16);
+      }
     }
-    for (int i = tid; i < 2 * 3 * FIR_PAIRS; i += FIR_THREADS) {
-      const int q = i / (3 * FIR_PAIRS), wd = i % (3 * FIR_PAIRS);
-      const long long t = (long long)r - 2 + q;
-      const uint32_t lo = bf16_bits(z_at(A, seg, t, 3 * c0 + 2 * wd));
-      const uint32_t hi = bf16_bits(z_at(A, seg, t, 3 * c0 + 2 * wd + 1));
-      S.zh[q][wd] = lo | (hi << 16);
+    if (nt.n > 0) cp_async_wait<1>(); else cp_async_wait<0>();
+    __syncthreads();
+
+    const int n = t.n, r = t.r;
+    // ---- K=3 short filter on channel pairs, sliding over 8 consecutive rows
+    const int g0 = rg * FIR_RPT;
+    if (g0 < n) {
+      bf162 w[3][3];
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int k = 0; k < 3; ++k) w[c][k] = S.sw[c][k][pp];
+      bf162 h2[3], h1[3];
+      {
+        const uint32_t* a = g0 >= 2 ? &S.zt[buf][g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
+        const uint32_t* b = g0 >= 1 ? &S.zt[buf][g0 - 1][3 * pp] : &S.zh[1][3 * pp];
+        split_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
+        split_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
+      }
+#pragma unroll
+      for (int i = 0; i < FIR_RPT; ++i) {
+        const int row = g0 + i;
+        if (row < n) {
+          bf162 cur[3], o[3];
+          split_triples(S.zt[buf][row][3 * pp], S.zt[buf][row][3 * pp + 1],
+                        S.zt[buf][row][3 * pp + 2], cur[0], cur[1], cur[2]);
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
+            h2[c] = h1[c];
+            h1[c] = cur[c];
+          }
+          S.ring[(r + row) & (FIR_RING - 1)][pp] = f2_from_bf162(__hmul2(o[1], o[2]));
+          S.x2s[row][pp] = o[0];
+        }
+      }
     }
     __syncthreads();
 
-    const int end = min(seg.e, r1);
-    while (r < end) {
-      const int n = min(FIR_BT, end - r);
-      // ---- stage z rows [r, r+n) x 192 columns (16-byte vectors)
-      constexpr int VPR = 3 * FIR_CG * 2 / 16;  // vectors per row
-      for (int i = tid; i < n * VPR; i += FIR_THREADS) {
-        const int row = i / VPR, v = i % VPR;
-        const uint4 val = __ldg(reinterpret_cast<const uint4*>(z + (long long)(r + row) * A.ldz +
-                                                               3 * c0) + v);
-        *(reinterpret_cast<uint4*>(&S.zt[row][0]) + v) = val;
+    // ---- z history for the next tile (reads zt/zh only; ring untouched)
+    if (tid < FIR_WORDS) {
+      uint32_t h0v, h1v;
+      if (n >= 2) {
+        h0v = S.zt[buf][n - 2][tid];
+        h1v = S.zt[buf][n - 1][tid];
+      } else {
+        h0v = S.zh[1][tid];
+        h1v = S.zt[buf][0][tid];
       }
-      __syncthreads();
-
-      // ---- K=3 short filter on channel pairs, sliding over 8 consecutive rows
-      const int g0 = rg * FIR_RPT;
-      if (g0 < n) {
-        bf162 w[3][3];
-#pragma unroll
-        for (int c = 0; c < 3; ++c)
-#pragma unroll
-          for (int t = 0; t < 3; ++t) w[c][t] = S.sw[c][t][pp];
-        bf162 h2[3], h1[3];
-        {
-          const uint32_t* a = g0 >= 2 ? &S.zt[g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
-          const uint32_t* b = g0 >= 1 ? &S.zt[g0 - 1][3 * pp] : &S.zh[1][3 * pp];
-          split_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
-          split_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
-        }
-        int ri = (r + g0) % RING;
-#pragma unroll
-        for (int i = 0; i < FIR_RPT; ++i) {
-          const int row = g0 + i;
-          if (row < n) {
-            bf162 cur[3], o[3];
-            split_triples(S.zt[row][3 * pp], S.zt[row][3 * pp + 1], S.zt[row][3 * pp + 2],
-                          cur[0], cur[1], cur[2]);
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-              o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
-              h2[c] = h1[c];
-              h1[c] = cur[c];
-            }
-            S.ring[ri][pp] = unpack2(__hmul2(o[1], o[2]));
-            S.x2s[row][pp] = o[0];
-          }
-          ri = ri + 1 == RING ? 0 : ri + 1;
-        }
-      }
-      __syncthreads();
-
-      // ---- z history for the next tile (reads zt/zh only; ring untouched)
-      if (tid < 3 * FIR_PAIRS) {
-        uint32_t h0v, h1v;
-        if (n >= 2) {
-          h0v = S.zt[n - 2][tid];
-          h1v = S.zt[n - 1][tid];
-        } else {
-          h0v = S.zh[1][tid];
-          h1v = S.zt[0][tid];
-        }
-        S.zh[0][tid] = h0v;
-        S.zh[1][tid] = h1v;
-      }
-
-      // ---- inner FIR over the ring: thread = (channel pair, rows i0..i0+7)
-      const int i0 = rg * FIR_RPT;
-      if (i0 < n) {
-        float2 acc[FIR_RPT];
-#pragma unroll
-        for (int q = 0; q < FIR_RPT; ++q) acc[q] = make_float2(0.f, 0.f);
-        int idx0 = (r + i0 - HIST) % RING;
-        idx0 += idx0 < 0 ? RING : 0;
-        float2 cur[8], nxt[8];
-#pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          int id = idx0 + x;
-          id -= id >= RING ? RING : 0;
-          cur[x] = S.ring[id][pp];
-        }
-#pragma unroll
-        for (int kb = 0; kb < K; kb += 8) {
-#pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            if (kb + 8 + x < HIST + FIR_RPT) {
-              int id = idx0 + kb + 8 + x;
-              id -= id >= RING ? RING : 0;
-              nxt[x] = S.ring[id][pp];
-            }
-          }
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            if (kb + kk < K) {
-              const float2 wv = unpack2(S.wsm[kb + kk][pp]);
-#pragma unroll
-              for (int q = 0; q < FIR_RPT; ++q) {
-                const float2 uv = (q + kk < 8) ? cur[q + kk] : nxt[q + kk - 8];
-                acc[q] = ffma2(wv, uv, acc[q]);
-              }
-            }
-          }
-#pragma unroll
-          for (int x = 0; x < 8; ++x) cur[x] = nxt[x];
-        }
-        const bool has_d = Dg != nullptr;
-        const bf162 d2 = S.dsm[pp];
-        bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + i0) * A.ldo + c0) + pp;
-        const long long ld2 = A.ldo / 2;
-#pragma unroll
-        for (int q = 0; q < FIR_RPT; ++q) {
-          if (i0 + q < n) {
-            bf162 y = pack2_rn(acc[q]);
-            if (has_d) {
-              int id = idx0 + q + HIST;
-              id -= id >= RING ? RING : 0;
-              y = __hadd2(y, __hmul2(d2, pack2_rn(S.ring[id][pp])));
-            }
-            outp[q * ld2] = __hmul2(S.x2s[i0 + q][pp], y);
-          }
-        }
-      }
-      __syncthreads();
-      r += n;
+      S.zh[0][tid] = h0v;
+      S.zh[1][tid] = h1v;
     }
-    ++j;
+
+    // ---- inner FIR over the ring: thread = (channel pair, rows i0..i0+7)
+    const int i0 = rg * FIR_RPT;
+    if (i0 < n) {
+      f2 acc[FIR_RPT];
+#pragma unroll
+      for (int q = 0; q < FIR_RPT; ++q) acc[q] = 0ull;  // +0.0f in both lanes
+      const int base = r + i0 - HIST;  // may be negative: masked arithmetic wraps
+      f2 cur[8], nxt[8];
+#pragma unroll
+      for (int x = 0; x < 8; ++x) cur[x] = S.ring[(base + x) & (FIR_RING - 1)][pp];
+#pragma unroll
+      for (int kb = 0; kb < K; kb += 8) {
+#pragma unroll
+        for (int x = 0; x < 8; ++x)
+          if (kb + 8 + x < HIST + FIR_RPT) nxt[x] = S.ring[(base + kb + 8 + x) & (FIR_RING - 1)][pp];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          if (kb + kk < K) {
+            const f2 wv = S.wsm[kb + kk][pp];
+#pragma unroll
+            for (int q = 0; q < FIR_RPT; ++q)
+              acc[q] = f2_fma(wv, (q + kk < 8) ? cur[q + kk] : nxt[q + kk - 8], acc[q]);
+          }
+        }
+#pragma unroll
+        for (int x = 0; x < 8; ++x) cur[x] = nxt[x];
+      }
+      const bool has_d = Dg != nullptr;
+      const bf162 d2 = S.dsm[pp];
+      bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + i0) * A.ldo + c0) + pp;
+      const long long ld2 = A.ldo / 2;
+#pragma unroll
+      for (int q = 0; q < FIR_RPT; ++q) {
+        if (i0 + q < n) {
+          bf162 y = bf162_from_f2(acc[q]);
+          if (has_d)
+            y = __hadd2(y, __hmul2(d2, bf162_from_f2(S.ring[(r + i0 + q) & (FIR_RING - 1)][pp])));
+          outp[q * ld2] = __hmul2(S.x2s[i0 + q][pp], y);
+        }
+      }
+    }
+    __syncthreads();
+    buf ^= 1;
+    t = nt;
   }
 }
 
@@ -415,10 +427,10 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
     attr_set = true;
   }
   // Rows per CTA: long enough that the (K-1)-row halo is a small fraction,
-  // short enough to fill the 148 SMs.
+  // short enough to fill the 148 SMs several times over.
   const int groups = P.H / FIR_CG;
-  int rows = K > 16 ? 1024 : 256;
-  const long long want_ctas = 148LL * 2 * 3;  // ~3 waves of 2 CTAs per SM
+  int rows = K > 16 ? 2048 : 1024;
+  const long long want_ctas = 148LL * 4;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
   dim3 grid((A.T + rows - 1) / rows, groups);
   fir_prefill_kernel<K><<<grid, FIR_THREADS, smem, st>>>(P, A, rows);

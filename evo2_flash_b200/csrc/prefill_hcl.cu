@@ -199,13 +199,24 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
   }
 }
 
-__device__ __forceinline__ void load_pole_pairs(const hyena_layer_params& P, int h, float2* p2,
-                                                float scale) {
+__device__ __forceinline__ void load_pole_pairs(const hyena_layer_params& P, int h, f2* p2) {
   const float* lp = P.log_poles + (long long)h * P.lp_stride_h;
 #pragma unroll
   for (int i = 0; i < HCL_S / 2; ++i)
-    p2[i] = make_float2(expf(lp[(2 * i) * P.lp_stride_s] * scale),
-                        expf(lp[(2 * i + 1) * P.lp_stride_s] * scale));
+    p2[i] = f2_make(expf(lp[(2 * i) * P.lp_stride_s]), expf(lp[(2 * i + 1) * P.lp_stride_s]));
+}
+
+// modal_readout16 on mode pairs (s2[i] = modes 2i, 2i+1): the same halving tree.
+__device__ __forceinline__ float readout_pairs(const f2* s2, const f2* r2) {
+  f2 p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = f2_mul(s2[i], r2[i]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = f2_add(p[i], p[i + 4]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) p[i] = f2_add(p[i], p[i + 2]);
+  const float2 v = f2_split(f2_add(p[0], p[1]));
+  return add_rn(v.x, v.y);
 }
 
 __global__ void __launch_bounds__(HCL_CG)
@@ -217,19 +228,18 @@ hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, Hcl
   const int c0 = blockIdx.y * HCL_CG;
   const int h = c0 + threadIdx.x;
   if (c.init && (c.blk < 0 || c.blk >= A.conv_state.num_blocks)) c.init = false;
-  float2 p2[HCL_S / 2], acc[HCL_S / 2];
-  load_pole_pairs(P, h, p2, 1.0f);
+  f2 p2[HCL_S / 2], acc[HCL_S / 2];
+  load_pole_pairs(P, h, p2);
 #pragma unroll
-  for (int i = 0; i < HCL_S / 2; ++i) acc[i] = make_float2(0.f, 0.f);
+  for (int i = 0; i < HCL_S / 2; ++i) acc[i] = 0ull;
   walk_chunk(A, P, c, c0, S, [&](int, float, float u) {
-    const float2 uu = make_float2(u, u);
+    const f2 uu = f2_make(u, u);
 #pragma unroll
-    for (int i = 0; i < HCL_S / 2; ++i) acc[i] = fadd2(fmul2(acc[i], p2[i]), uu);
+    for (int i = 0; i < HCL_S / 2; ++i) acc[i] = f2_add(f2_mul(acc[i], p2[i]), uu);
   });
-  float4* dst = reinterpret_cast<float4*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
+  f2* dst = reinterpret_cast<f2*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
 #pragma unroll
-  for (int i = 0; i < HCL_S / 4; ++i)
-    dst[i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+  for (int i = 0; i < HCL_S / 2; ++i) dst[i] = acc[i];
 }
 
 // One thread per (segment, channel, mode): S_in for every chunk, written over
@@ -275,30 +285,25 @@ hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWor
   const bool blk_ok = c.blk >= 0 && c.blk < A.inner_state.num_blocks &&
                       c.blk < A.conv_state.num_blocks;
   if (c.init && !blk_ok) c.init = false;
-  float2 p2[HCL_S / 2], r2[HCL_S / 2], s2[HCL_S / 2];
-  load_pole_pairs(P, h, p2, 1.0f);
+  f2 p2[HCL_S / 2], r2[HCL_S / 2], s2[HCL_S / 2];
+  load_pole_pairs(P, h, p2);
   {
     const float* rr = P.residues + (long long)h * P.res_stride_h;
 #pragma unroll
     for (int i = 0; i < HCL_S / 2; ++i)
-      r2[i] = make_float2(rr[(2 * i) * P.res_stride_s], rr[(2 * i + 1) * P.res_stride_s]);
-    const float4* src =
-        reinterpret_cast<const float4*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
+      r2[i] = f2_make(rr[(2 * i) * P.res_stride_s], rr[(2 * i + 1) * P.res_stride_s]);
+    const f2* src = reinterpret_cast<const f2*>(W.states + ((long long)blockIdx.x * P.H + h) * HCL_S);
 #pragma unroll
-    for (int i = 0; i < HCL_S / 4; ++i) {
-      const float4 v = src[i];
-      s2[2 * i] = make_float2(v.x, v.y);
-      s2[2 * i + 1] = make_float2(v.z, v.w);
-    }
+    for (int i = 0; i < HCL_S / 2; ++i) s2[i] = src[i];
   }
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float d = Dg ? ldbf(Dg + h) : 0.0f;
   bf16* out = static_cast<bf16*>(A.out);
   walk_chunk(A, P, c, c0, S, [&](int row, float x2, float u) {
-    const float2 uu = make_float2(u, u);
+    const f2 uu = f2_make(u, u);
 #pragma unroll
-    for (int i = 0; i < HCL_S / 2; ++i) s2[i] = fadd2(fmul2(s2[i], p2[i]), uu);
-    float y = bf16r(modal_readout16_x2(s2, r2));
+    for (int i = 0; i < HCL_S / 2; ++i) s2[i] = f2_add(f2_mul(s2[i], p2[i]), uu);
+    float y = bf16r(readout_pairs(s2, r2));
     if (Dg) y = bf16r(y + bf16r(u * d));
     out[(long long)row * A.ldo + h] = __float2bfloat16_rn(bf16r(y * x2));
   });
@@ -311,8 +316,9 @@ hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWor
 #pragma unroll
     for (int i = 0; i < HCL_S / 2; ++i) {
       const long long b = c.blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride;
-      st[b + (long long)(2 * i) * A.inner_state.col_stride] = s2[i].x;
-      st[b + (long long)(2 * i + 1) * A.inner_state.col_stride] = s2[i].y;
+      const float2 v = f2_split(s2[i]);
+      st[b + (long long)(2 * i) * A.inner_state.col_stride] = v.x;
+      st[b + (long long)(2 * i + 1) * A.inner_state.col_stride] = v.y;
     }
   }
 }
