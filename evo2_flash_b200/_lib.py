@@ -13,7 +13,7 @@ from ._build import LIB_PATH
 
 HYENA_KIND_FIR = 0
 HYENA_KIND_IIR = 1
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class StateView(C.Structure):
@@ -103,10 +103,11 @@ SIGNATURES = {
                                    C.c_int32, C.c_void_p, C.c_void_p]),
     "hyena_gemm_e4m3": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                   C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
-                                  C.c_void_p, C.c_void_p]),
+                                  C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "hyena_gemm_bf16": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p,
                                   C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
-                                  C.c_void_p]),
+                                  C.c_void_p, C.c_size_t, C.c_void_p]),
+    "hyena_gemm_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
 }
 
 _lock = threading.Lock()

@@ -29,9 +29,11 @@ int quant_e4m3_launch(const void* x, int64_t ldx, void* q, int64_t ldq, int M, i
                       const float* scale, cudaStream_t st);
 int gemm_e4m3_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                      int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
-                     cudaStream_t st);
+                     void* ws, size_t ws_bytes, cudaStream_t st);
 int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
-                     int64_t ldo, int M, int N, int K, const void* bias, cudaStream_t st);
+                     int64_t ldo, int M, int N, int K, const void* bias, void* ws,
+                     size_t ws_bytes, cudaStream_t st);
+size_t gemm_workspace_size(int M, int N, int K, bool fp8);
 
 static int check_params(const hyena_layer_params* p) {
   HB_REQUIRE(p != nullptr, "null layer params");
@@ -120,18 +122,24 @@ int hyena_quant_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, int32_t M
 
 int hyena_gemm_e4m3(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                     int64_t ldo, int32_t M, int32_t N, int32_t K, const float* scale_a,
-                    const float* scale_b, void* stream) {
+                    const float* scale_b, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   HB_REQUIRE(A && B && out && scale_a && scale_b, "null gemm pointer");
-  return gemm_e4m3_launch(A, lda, B, ldb, out, ldo, M, N, K, scale_a, scale_b,
-                          static_cast<cudaStream_t>(stream));
+  return gemm_e4m3_launch(A, lda, B, ldb, out, ldo, M, N, K, scale_a, scale_b, workspace,
+                          workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                     int64_t ldo, int32_t M, int32_t N, int32_t K, const void* bias,
-                    void* stream) {
+                    void* workspace, size_t workspace_bytes, void* stream) {
   HB_REQUIRE(A && B && out, "null gemm pointer");
-  return gemm_bf16_launch(A, lda, B, ldb, out, ldo, M, N, K, bias,
+  return gemm_bf16_launch(A, lda, B, ldb, out, ldo, M, N, K, bias, workspace, workspace_bytes,
                           static_cast<cudaStream_t>(stream));
+}
+
+size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return gemm_workspace_size(M, N, K, fp8 != 0);
 }
 
 }  // extern "C"

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
             const float* __restrict__ sa, const float* __restrict__ sb,
-            const bf16* __restrict__ bias) {
+            const bf16* __restrict__ bias, int splits, float* __restrict__ ws) {
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = Cfg<BN>::TMEM_COLS;
@@ -181,7 +181,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   // whole weight (<= 50 MB at the 7B shape) stays in L2 while the activations
   // stream through once.
   const int n_tiles = (N + BN - 1) / BN;
-  const int total = n_tiles * ((M + BM - 1) / BM);
+  // Work units: (tile, K slice).  splits > 1 (small M only) sums the slices'
+  // fp32 partials into `ws`; a finalize kernel applies scale / bias.
+  const int total = n_tiles * ((M + BM - 1) / BM) * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -212,9 +214,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+        const int tile = unit / splits, sp = unit % splits;
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int kb1 = (sp + 1) * kblocks / splits;
+        for (int kb = sp * kblocks / splits; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) { ok = false; break; }
           mbar_expect_tx(&S.full[s], STAGE_BYTES);
@@ -231,12 +235,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       constexpr uint32_t ID = idesc<FP8, BN>();
       uint32_t it = 0, ti = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++ti) {
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++ti) {
+        const int sp = unit % splits;
+        const int kb0 = sp * kblocks / splits, kb1 = (sp + 1) * kblocks / splits;
         const int b = ti & 1;
         if (!mbar_wait(&S.acc_empty[b], ((ti >> 1) & 1) ^ 1)) ok = false;
         fence_after();
         const uint32_t d = tmem + uint32_t(b * BN);
-        for (int kb = 0; kb < kblocks && ok; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&S.full[s], (it / STAGES) & 1)) { ok = false; break; }
           fence_after();
@@ -244,7 +250,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           for (int kk = 0; kk < BKB / 32; ++kk) {
             const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
             const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
-            mma<FP8>(d, ad, bd, ID, (kb | kk) != 0 ? 1u : 0u);
+            mma<FP8>(d, ad, bd, ID, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&S.empty[s]);
         }
@@ -259,7 +265,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       scale_b = __ldg(sb);
     }
     uint32_t ti = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++ti) {
+      const int tile = unit / splits;
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int b = ti & 1;
       const bool ok = mbar_wait(&S.acc_full[b], (ti >> 1) & 1);
@@ -277,6 +284,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         const int col0 = n0 + cb * 32;
         if (row >= M || col0 >= N) continue;
+        if (splits > 1) {  // K-slice partial: vector reduction into the fp32 workspace
+          float* wrow = ws + (long long)row * N + col0;
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            if (col0 + 4 * v >= N) break;
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + 4 * v),
+                         "f"(__uint_as_float(r[4 * v])), "f"(__uint_as_float(r[4 * v + 1])),
+                         "f"(__uint_as_float(r[4 * v + 2])), "f"(__uint_as_float(r[4 * v + 3]))
+                         : "memory");
+          }
+          continue;
+        }
         bf16* dst = out + (long long)row * ldo + col0;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
@@ -315,6 +334,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
+// out = bf16((ws * sa) * sb) or bf16(ws + bias): the split-K epilogue.
+__global__ void __launch_bounds__(256)
+splitk_finalize_kernel(const float* __restrict__ ws, bf16* __restrict__ out, int64_t ldo, int M,
+                       int N, const float* __restrict__ sa, const float* __restrict__ sb,
+                       const bf16* __restrict__ bias) {
+  const int vpr = N / 4;
+  const long long total = (long long)M * vpr;
+  const float a = sa ? __ldg(sa) : 1.0f, b = sb ? __ldg(sb) : 1.0f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / vpr;
+    const int c = int(i % vpr) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(ws + row * N + c);
+    float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (sa) x[e] = (x[e] * a) * b;
+      if (bias) x[e] += __bfloat162float(bias[c + e]);
+    }
+    const __nv_bfloat162 p = __floats2bfloat162_rn(x[0], x[1]);
+    const __nv_bfloat162 q = __floats2bfloat162_rn(x[2], x[3]);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&p);
+    o.y = *reinterpret_cast<const uint32_t*>(&q);
+    *reinterpret_cast<uint2*>(out + row * ldo + c) = o;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -347,10 +394,21 @@ static int make_map(CUtensorMap* m, const void* base, bool fp8, uint64_t inner, 
   return HYENA_OK;
 }
 
+static int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+  }
+  return sms;
+}
+
 template <bool FP8, int BN>
 static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* out, int64_t ldo,
                      int M, int N, int K, const float* sa, const float* sb, const void* bias,
-                     cudaStream_t st) {
+                     int splits, float* ws, cudaStream_t st) {
   CUtensorMap tb;
   int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
   if (rc) return rc;
@@ -362,34 +420,51 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
       return check_launch("cudaFuncSetAttribute(gemm)");
     attr = true;
   }
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-      sms = 148;
-  }
-  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
-  dim3 grid((unsigned)(tiles < sms ? tiles : sms));
+  if (splits > 1 && cudaMemsetAsync(ws, 0, sizeof(float) * (size_t)M * N, st) != cudaSuccess)
+    return check_launch("cudaMemsetAsync(split-K workspace)");
+  const long long units = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM) * splits;
+  dim3 grid((unsigned)(units < num_sms() ? units : num_sms()));
   gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
-                                                    K, sa, sb, static_cast<const bf16*>(bias));
-  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+                                                    K, sa, sb, static_cast<const bf16*>(bias),
+                                                    splits, ws);
+  rc = check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+  if (rc || splits == 1) return rc;
+  long long blocks = ((long long)M * (N / 4) + 255) / 256;
+  if (blocks > 4LL * num_sms()) blocks = 4LL * num_sms();
+  splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ws, static_cast<bf16*>(out), ldo, M, N,
+                                                           sa, sb, static_cast<const bf16*>(bias));
+  return check_launch("splitk_finalize_kernel");
 }
 
-// N-tile choice: the widest tile that still gives at least one CTA per SM
-// (148 on B200); small-M (decode) GEMMs get narrow tiles and more CTAs.
-static int pick_bn(int M, int N) {
+struct Plan {
+  int bn, splits;
+};
+
+static bool mt_cover(int M, int N) {
+  return (long long)((M + BM - 1) / BM) * ((N + 63) / 64) >= num_sms();
+}
+
+// Large M: the widest N-tile that still gives every SM a tile, unsplit.
+// Small M (decode batches): 256-wide tiles with K split so that tiles x slices
+// cover the SMs once, each slice at least two K stages long.
+static Plan plan(int M, int N, int K, bool fp8) {
   const long long mt = (M + BM - 1) / BM;
-  for (int bn : {256, 128, 64}) {
-    if (mt * ((N + bn - 1) / bn) >= 148) return bn;
+  const int sms = num_sms();
+  for (int bn : {256, 128}) {
+    if (mt * ((N + bn - 1) / bn) >= sms) return {bn, 1};
   }
-  return 32;
+  const int kblocks = K / (BKB / (fp8 ? 1 : 2));
+  const long long tiles = mt * ((N + 255) / 256);
+  long long sp = sms / tiles;
+  if (sp > kblocks / 2) sp = kblocks / 2;
+  if (sp >= 2 && N % 4 == 0) return {256, (int)sp};
+  return {mt * ((N + 63) / 64) >= sms ? 64 : 32, 1};
 }
 
 template <bool FP8>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out, int64_t ldo,
                   int M, int N, int K, const float* sa, const float* sb, const void* bias,
-                  cudaStream_t st) {
+                  void* ws, size_t ws_bytes, cudaStream_t st) {
   if (M <= 0 || N <= 0) return HYENA_OK;
   const int KE = BKB / (FP8 ? 1 : 2);
   HB_REQUIRE(K > 0 && K % KE == 0, FP8 ? "e4m3 GEMM needs K % 128 == 0" : "bf16 GEMM needs K % 64 == 0");
@@ -401,11 +476,15 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   CUtensorMap ta;
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
-  switch (pick_bn(M, N)) {
-    case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
-    case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
-    case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
-    default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+  Plan pl = plan(M, N, K, FP8);
+  if (pl.splits > 1 && (ws == nullptr || ws_bytes < sizeof(float) * (size_t)M * N || !aligned16(ws)))
+    pl = {mt_cover(M, N) ? 64 : 32, 1};
+  float* w = static_cast<float*>(ws);
+  switch (pl.bn) {
+    case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, w, st);
+    case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
+    case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
+    default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
   }
 }
 
@@ -413,13 +492,20 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
 
 int gemm_e4m3_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                      int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
-                     cudaStream_t st) {
-  return gemm::launch<true>(A, lda, B, ldb, out, ldo, M, N, K, sa, sb, nullptr, st);
+                     void* ws, size_t ws_bytes, cudaStream_t st) {
+  return gemm::launch<true>(A, lda, B, ldb, out, ldo, M, N, K, sa, sb, nullptr, ws, ws_bytes, st);
 }
 
 int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
-                     int64_t ldo, int M, int N, int K, const void* bias, cudaStream_t st) {
-  return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, st);
+                     int64_t ldo, int M, int N, int K, const void* bias, void* ws,
+                     size_t ws_bytes, cudaStream_t st) {
+  return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, ws,
+                             ws_bytes, st);
+}
+
+size_t gemm_workspace_size(int M, int N, int K, bool fp8) {
+  const gemm::Plan p = gemm::plan(M, N, K, fp8);
+  return p.splits > 1 ? sizeof(float) * (size_t)M * N : 0;
 }
 
 }  // namespace hb

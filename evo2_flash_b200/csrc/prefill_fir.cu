@@ -19,16 +19,16 @@
 
 namespace hb {
 
-constexpr int FIR_CG = 64;       // channels per CTA
+constexpr int FIR_CG = 32;       // channels per CTA (two CTAs share an SM)
 constexpr int FIR_PAIRS = FIR_CG / 2;
 constexpr int FIR_BT = 128;      // rows per tile
-constexpr int FIR_THREADS = 512;
+constexpr int FIR_THREADS = 256;
 constexpr int FIR_RPT = 8;       // rows per thread in the gate and tap phases
 constexpr int FIR_RING = 256;    // u ring rows (power of two >= K-1 + FIR_BT)
 constexpr int FIR_WORDS = 3 * FIR_PAIRS;  // bf16x2 words of z per row per CTA
 constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
 
-// Thread (pair p = tid % 32, row group g = tid / 32) owns channels c0+2p, c0+2p+1
+// Thread (pair p = tid % 16, row group g = tid / 16) owns channels c0+2p, c0+2p+1
 // and tile rows 8g .. 8g+7 in both the gate and the tap phases.
 template <int K>
 struct FirShared {
@@ -141,7 +141,7 @@ __device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefi
 }
 
 template <int K>
-__global__ void __launch_bounds__(FIR_THREADS, 1)
+__global__ void __launch_bounds__(FIR_THREADS, 2)
 fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
   constexpr int HIST = K - 1;
   static_assert(HIST + FIR_BT <= FIR_RING, "ring too small");
@@ -185,7 +185,7 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
                     : __floats2bfloat162_rn(0.f, 0.f);
 
   const int pp = tid % FIR_PAIRS;  // channel pair
-  const int rg = tid / FIR_PAIRS;  // row group 0..15
+  const int rg = tid / FIR_PAIRS;  // row group 0..15 (FIR_BT / FIR_RPT)
   float* ring_f = reinterpret_cast<float*>(&S.ring[0][0]);
   int cur_seg = -1;
 
@@ -430,7 +430,7 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   // short enough to fill the 148 SMs several times over.
   const int groups = P.H / FIR_CG;
   int rows = K > 16 ? 2048 : 1024;
-  const long long want_ctas = 148LL * 4;
+  const long long want_ctas = 148LL * 8;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
   dim3 grid((A.T + rows - 1) / rows, groups);
   fir_prefill_kernel<K><<<grid, FIR_THREADS, smem, st>>>(P, A, rows);

@@ -256,10 +256,18 @@ def gemm_e4m3(a, b, scale_a, scale_b, out=None):
     if out is None:
         out = torch.empty(M, N, dtype=BF16, device=a.device)
     lib = _lib.load()
+    ws = _gemm_workspace(lib, M, N, K, True, a.device)
     _lib.check(lib.hyena_gemm_e4m3(_ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out),
                                    out.stride(0), M, N, K, _ptr(scale_a), _ptr(scale_b),
+                                   _ptr(ws), C.c_size_t(0 if ws is None else ws.numel() * 4),
                                    _stream()), "hyena_gemm_e4m3")
     return out
+
+
+def _gemm_workspace(lib, M, N, K, fp8, device):
+    """fp32 split-K workspace for small-M GEMMs (torch caching allocator)."""
+    n = lib.hyena_gemm_workspace_size(M, N, K, int(fp8))
+    return torch.empty(n // 4, dtype=torch.float32, device=device) if n else None
 
 
 def gemm_bf16(a, b, bias=None, out=None):
@@ -273,7 +281,9 @@ def gemm_bf16(a, b, bias=None, out=None):
     if out is None:
         out = torch.empty(M, N, dtype=BF16, device=a.device)
     lib = _lib.load()
+    ws = _gemm_workspace(lib, M, N, K, False, a.device)
     _lib.check(lib.hyena_gemm_bf16(_ptr(a), a.stride(0), _ptr(b), b.stride(0), _ptr(out),
-                                   out.stride(0), M, N, K, _ptr(bias), _stream()),
+                                   out.stride(0), M, N, K, _ptr(bias), _ptr(ws),
+                                   C.c_size_t(0 if ws is None else ws.numel() * 4), _stream()),
                "hyena_gemm_bf16")
     return out

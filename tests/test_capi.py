@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol(lib):
     for name in declared_symbols():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.hyena_abi_version() == 1
+    assert lib.hyena_abi_version() == _lib.ABI_VERSION
 
 
 def test_invalid_arguments_are_rejected_on_host(lib):
@@ -51,7 +51,7 @@ def test_invalid_arguments_are_rejected_on_host(lib):
     p.H, p.K = 128, 9  # unsupported taps
     assert lib.hyena_prefill(C.byref(p), C.byref(a), None, 0, None) == 1
     # null GEMM operands
-    assert lib.hyena_gemm_bf16(None, 64, None, 64, None, 64, 1, 8, 64, None, None) == 1
+    assert lib.hyena_gemm_bf16(None, 64, None, 64, None, 64, 1, 8, 64, None, None, 0, None) == 1
 
 
 def test_empty_work_is_a_no_op(lib):
@@ -75,3 +75,10 @@ def test_workspace_size_only_for_li(lib):
     p.kind, p.K = 1, 16
     n = lib.hyena_prefill_workspace_size(C.byref(p), 65536, 8)
     assert n >= (65536 // 256) * 4096 * 16 * 4
+
+
+def test_gemm_workspace_only_for_small_m(lib):
+    # decode-sized GEMMs split K (need fp32 workspace); prefill-sized ones do not
+    assert lib.hyena_gemm_workspace_size(128, 12288, 4096, 1) == 128 * 12288 * 4
+    assert lib.hyena_gemm_workspace_size(65536, 12288, 4096, 1) == 0
+    assert lib.hyena_gemm_workspace_size(0, 12288, 4096, 1) == 0
