@@ -98,6 +98,8 @@ SIGNATURES = {
     "hyena_prefill_workspace_size": (C.c_size_t, [C.POINTER(LayerParams), C.c_int32, C.c_int32]),
     "hyena_prefill": (C.c_int, [C.POINTER(LayerParams), C.POINTER(PrefillArgs), C.c_void_p,
                                 C.c_size_t, C.c_void_p]),
+    "hyena_prefill_noalloc": (C.c_int, [C.POINTER(LayerParams), C.POINTER(PrefillArgs),
+                                        C.c_void_p]),
     "hyena_decode": (C.c_int, [C.POINTER(LayerParams), C.POINTER(DecodeArgs), C.c_void_p]),
     "hyena_quant_e4m3": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int32,
                                    C.c_int32, C.c_void_p, C.c_void_p]),

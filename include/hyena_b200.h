@@ -111,6 +111,17 @@ HYENA_API size_t hyena_prefill_workspace_size(const hyena_layer_params* p, int32
 HYENA_API int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_args* a,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+/* Prefill for callers that cannot allocate device memory.  No counterpart in
+ * the reference (its Python path allocates through torch).  Same arguments and
+ * result as hyena_prefill minus the workspace: the LI kind's scratch is a fixed
+ * 32 MiB array inside this library, present on every GPU that loads it until the
+ * process exits.  LI prefills needing more (beyond ~32K packed tokens at
+ * H = 4096) fail with HYENA_ERR_INVALID.  The first call on a device looks up
+ * the array's device address; make it before any stream capture.  All calls
+ * share the array: calls whose kernels overlap on the GPU race on it. */
+HYENA_API int hyena_prefill_noalloc(const hyena_layer_params* p, const hyena_prefill_args* a,
+                                    void* stream);
+
 /* ---------------------------------------------------------------- decode / verify
  * Replaces, for the decode rows of one step:
  *   ordinary decode: triton_decode.hyena_decode (triton_decode.py:56-211) and the
