@@ -51,7 +51,6 @@ struct __align__(1024) Smem {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
-  int last_unit;  // split-K: this CTA finished the tile's last slice
 };
 
 __device__ int g_wait_timeouts;
@@ -160,35 +159,6 @@ template <bool FP8, int BN>
 __host__ __device__ constexpr uint32_t idesc() {
   return (1u << 4) | ((FP8 ? 0u : 1u) << 7) | ((FP8 ? 0u : 1u) << 10) |
          (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
-}
-
-// 32 fp32 accumulators of one output row -> bf16 with the GEMM's epilogue:
-// (acc * sa) * sb (fp8_emul.py:87) for e4m3, acc + bias for bf16.
-template <bool FP8>
-__device__ __forceinline__ void store_row32(bf16* dst, const uint32_t (&r)[32], int cols_left,
-                                            int col0, float scale_a, float scale_b,
-                                            const bf16* __restrict__ bias) {
-#pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    if (8 * v >= cols_left) break;
-    uint4 pk;
-    uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float x0 = __uint_as_float(r[8 * v + 2 * e]);
-      float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
-      if constexpr (FP8) {
-        x0 = (x0 * scale_a) * scale_b;
-        x1 = (x1 * scale_a) * scale_b;
-      } else if (bias != nullptr) {
-        x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
-        x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
-      }
-      const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-      pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
-    }
-    *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
-  }
 }
 
 template <bool FP8, int BN>
@@ -300,10 +270,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int b = ti & 1;
       const bool ok = mbar_wait(&S.acc_full[b], (ti >> 1) & 1);
-      // The MMA warp gave up: stop rather than time out per tile.  With split-K
-      // the four epilogue warps meet at a named barrier per unit, so they keep
-      // going (a few units per CTA) instead of leaving one another waiting.
-      if (!ok && splits == 1) break;
+      if (!ok) break;  // the MMA warp gave up: stop rather than time out per tile
       fence_after();
       const int row = m0 + 32 * q + lane;
 #pragma unroll 1
@@ -317,59 +284,41 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         const int col0 = n0 + cb * 32;
         if (row >= M || col0 >= N) continue;
-        if (splits > 1) {  // K-slice partial: plain stores into this slice's fp32 plane
-          float* wrow = ws + ((long long)(unit % splits) * M + row) * N + col0;
+        if (splits > 1) {  // K-slice partial: vector reduction into the fp32 workspace
+          float* wrow = ws + (long long)row * N + col0;
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
             if (col0 + 4 * v >= N) break;
-            *reinterpret_cast<float4*>(wrow + 4 * v) =
-                make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                            __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + 4 * v),
+                         "f"(__uint_as_float(r[4 * v])), "f"(__uint_as_float(r[4 * v + 1])),
+                         "f"(__uint_as_float(r[4 * v + 2])), "f"(__uint_as_float(r[4 * v + 3]))
+                         : "memory");
           }
           continue;
         }
-        store_row32<FP8>(out + (long long)row * ldo + col0, r, N - col0, col0, scale_a, scale_b,
-                         bias);
-      }
-      if (splits > 1) {
-        // The CTA that completes a tile's last slice sums the slices in slice
-        // order (deterministic) and writes the bf16 tile.
-        int* counters = reinterpret_cast<int*>(ws + (long long)splits * M * N);
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) {
-          __threadfence();
-          S.last_unit = atomicAdd(counters + tile, 1) == splits - 1;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (S.last_unit) {
-          __threadfence();
-          if (row < M) {
-#pragma unroll 1
-            for (int cb = 0; cb < BN / 32; ++cb) {
-              const int col0 = n0 + cb * 32;
-              if (col0 >= N) break;
-              float acc[32];
+        bf16* dst = out + (long long)row * ldo + col0;
 #pragma unroll
-              for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
-              for (int spl = 0; spl < splits; ++spl) {
-                const float* wrow = ws + ((long long)spl * M + row) * N + col0;
+        for (int v = 0; v < 4; ++v) {
+          if (col0 + 8 * v >= N) break;
+          uint4 pk;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                  if (col0 + 4 * v < N) {
-                    const float4 x = __ldcg(reinterpret_cast<const float4*>(wrow + 4 * v));
-                    acc[4 * v] += x.x; acc[4 * v + 1] += x.y;
-                    acc[4 * v + 2] += x.z; acc[4 * v + 3] += x.w;
-                  }
-                }
+          for (int e = 0; e < 4; ++e) {
+            float x0 = __uint_as_float(r[8 * v + 2 * e]);
+            float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
+            if constexpr (FP8) {
+              x0 = (x0 * scale_a) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+              x1 = (x1 * scale_a) * scale_b;
+            } else {
+              if (bias != nullptr) {
+                x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
+                x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
               }
-              uint32_t rr[32];
-#pragma unroll
-              for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(acc[e]);
-              store_row32<FP8>(out + (long long)row * ldo + col0, rr, N - col0, col0, scale_a,
-                               scale_b, bias);
             }
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+            pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          if (warp == 2 && lane == 0) counters[tile] = 0;  // ready for the next call
+          *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
         }
       }
     }
@@ -382,6 +331,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS)
                  : "memory");
+  }
+}
+
+// out = bf16((ws * sa) * sb) or bf16(ws + bias): the split-K epilogue.
+__global__ void __launch_bounds__(256)
+splitk_finalize_kernel(const float* __restrict__ ws, bf16* __restrict__ out, int64_t ldo, int M,
+                       int N, const float* __restrict__ sa, const float* __restrict__ sb,
+                       const bf16* __restrict__ bias) {
+  const int vpr = N / 4;
+  const long long total = (long long)M * vpr;
+  const float a = sa ? __ldg(sa) : 1.0f, b = sb ? __ldg(sb) : 1.0f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / vpr;
+    const int c = int(i % vpr) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(ws + row * N + c);
+    float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (sa) x[e] = (x[e] * a) * b;
+      if (bias) x[e] += __bfloat162float(bias[c + e]);
+    }
+    const __nv_bfloat162 p = __floats2bfloat162_rn(x[0], x[1]);
+    const __nv_bfloat162 q = __floats2bfloat162_rn(x[2], x[3]);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&p);
+    o.y = *reinterpret_cast<const uint32_t*>(&q);
+    *reinterpret_cast<uint2*>(out + row * ldo + c) = o;
   }
 }
 
@@ -443,27 +420,25 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
       return check_launch("cudaFuncSetAttribute(gemm)");
     attr = true;
   }
-  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
-  if (splits > 1 && cudaMemsetAsync(ws + (size_t)splits * M * N, 0, sizeof(int) * (size_t)tiles,
-                                    st) != cudaSuccess)
-    return check_launch("cudaMemsetAsync(split-K tile counters)");
-  const long long units = tiles * splits;
+  if (splits > 1 && cudaMemsetAsync(ws, 0, sizeof(float) * (size_t)M * N, st) != cudaSuccess)
+    return check_launch("cudaMemsetAsync(split-K workspace)");
+  const long long units = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM) * splits;
   dim3 grid((unsigned)(units < num_sms() ? units : num_sms()));
   gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
                                                     K, sa, sb, static_cast<const bf16*>(bias),
                                                     splits, ws);
-  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+  rc = check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+  if (rc || splits == 1) return rc;
+  long long blocks = ((long long)M * (N / 4) + 255) / 256;
+  if (blocks > 4LL * num_sms()) blocks = 4LL * num_sms();
+  splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ws, static_cast<bf16*>(out), ldo, M, N,
+                                                           sa, sb, static_cast<const bf16*>(bias));
+  return check_launch("splitk_finalize_kernel");
 }
 
 struct Plan {
   int bn, splits;
 };
-
-// split-K workspace: `splits` fp32 planes of M x N, then one int per tile.
-static size_t splitk_bytes(int M, int N, const Plan& p) {
-  const size_t tiles = (size_t)((N + p.bn - 1) / p.bn) * ((M + BM - 1) / BM);
-  return sizeof(float) * (size_t)p.splits * M * N + sizeof(int) * tiles;
-}
 
 static bool mt_cover(int M, int N) {
   return (long long)((M + BM - 1) / BM) * ((N + 63) / 64) >= num_sms();
@@ -502,7 +477,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
   Plan pl = plan(M, N, K, FP8);
-  if (pl.splits > 1 && (ws == nullptr || ws_bytes < splitk_bytes(M, N, pl) || !aligned16(ws)))
+  if (pl.splits > 1 && (ws == nullptr || ws_bytes < sizeof(float) * (size_t)M * N || !aligned16(ws)))
     pl = {mt_cover(M, N) ? 64 : 32, 1};
   float* w = static_cast<float*>(ws);
   switch (pl.bn) {
@@ -530,7 +505,7 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
 
 size_t gemm_workspace_size(int M, int N, int K, bool fp8) {
   const gemm::Plan p = gemm::plan(M, N, K, fp8);
-  return p.splits > 1 ? gemm::splitk_bytes(M, N, p) : 0;
+  return p.splits > 1 ? sizeof(float) * (size_t)M * N : 0;
 }
 
 }  // namespace hb
