@@ -96,13 +96,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+// TMA tile load with an L2 eviction-priority hint (createpolicy).
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
-                                            int x, int y) {
+                                            int x, int y, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// 16-byte store marked streaming (evict-first in L2): GEMM outputs are read
+// once, later, by another kernel, and must not push the weights out of L2.
+__device__ __forceinline__ void st_stream16(void* p, const uint4& v) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 __device__ __forceinline__ void fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -212,6 +230,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
   if (warp == 0) {
     if (lane == 0) {
+      // Many M tiles (prefill): the weight panel is reused by every M tile, the
+      // activations once per N tile -> keep B, stream A.  Few M tiles (decode):
+      // A is reused by every N tile, the weight streamed once per call.
+      const bool many_m = (M + BM - 1) / BM > 8;
+      const uint64_t pol_a = many_m ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = many_m ? policy_evict_last() : policy_evict_first();
       uint32_t it = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
@@ -222,8 +246,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           const int s = it % STAGES;
           if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) { ok = false; break; }
           mbar_expect_tx(&S.full[s], STAGE_BYTES);
-          tma_load_2d(&tmA, &S.full[s], S.a[s], kb * KE, m0);
-          tma_load_2d(&tmB, &S.full[s], S.b[s], kb * KE, n0);
+          tma_load_2d(&tmA, &S.full[s], S.a[s], kb * KE, m0, pol_a);
+          tma_load_2d(&tmB, &S.full[s], S.b[s], kb * KE, n0, pol_b);
         }
       }
       // Drain: every issued copy has landed before the CTA can exit.
@@ -318,7 +342,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
             pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
           }
-          *reinterpret_cast<uint4*>(dst + 8 * v) = pk;
+          st_stream16(dst + 8 * v, pk);
         }
       }
     }

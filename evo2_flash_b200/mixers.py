@@ -29,11 +29,11 @@ partial outputs before the bias.  State shapes shrink to the local H.
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 from torch import nn
 
 from . import ops
 from .forward_context import lookup
+from .parallel import all_reduce_partial, shard_mixer_tensors
 
 HYENA_MIXER_OP = "evo2_b200::hyena_mixer"
 
@@ -332,9 +332,7 @@ class HyenaMixerBase(nn.Module):
     def _out_proj(self, g):
         out, _ = self.out_proj(g)
         if self.tp_size > 1:
-            dist.all_reduce(out, group=self.tp_group)
-            if self.out_proj.bias is not None:
-                out = out + self.out_proj.bias
+            out = all_reduce_partial(out, self.out_proj.bias, self.tp_group)
         return out
 
     def _forward_impl(self, hidden_states, token_ids=None):
@@ -370,25 +368,15 @@ class HyenaMixerBase(nn.Module):
     # ---- weights ------------------------------------------------------------------
     def load_full_weights(self, tensors: dict):
         """Copies unsharded checkpoint tensors (names as in the reference) into this
-        rank's shard: in_proj rows and short_filter rows by whole triples, inner
-        parameters by channel, out_proj columns."""
-        hl, r = self.hidden, self.tp_rank
-        rows3 = slice(3 * hl * r, 3 * hl * (r + 1))
-        rows = slice(hl * r, hl * (r + 1))
+        rank's shard (evo2_flash_b200.parallel.shard_mixer_tensors)."""
+        shard = shard_mixer_tensors(tensors, self.tp_rank, self.tp_size, self.hidden_full)
+        params = dict(self.named_parameters())
         with torch.no_grad():
-            for name, t in tensors.items():
-                if name in ("in_proj.weight",):
-                    self.in_proj.weight.copy_(t[rows3])
-                elif name in ("in_proj.weight_scale", "in_proj.input_scale"):
-                    getattr(self.in_proj, name.split(".")[1]).copy_(t.reshape(1))
-                elif name == "short_filter":
-                    self.short_filter.copy_(t.reshape(-1, 1, self.k_short)[rows3])
-                elif name == "out_proj.weight":
-                    self.out_proj.weight.copy_(t[:, rows])
-                elif name == "out_proj.bias":
-                    self.out_proj.bias.copy_(t)
-                else:
-                    self._load_inner(name, t, rows)
+            for name, t in shard.items():
+                if name not in params:
+                    raise KeyError(f"unexpected tensor {name!r} for {type(self).__name__}")
+                dst = params[name]
+                dst.copy_(t.reshape(dst.shape))
         self._weights = None
 
 
@@ -422,13 +410,6 @@ class HyenaFIRMixer(HyenaMixerBase):
             s1 = s1.transpose(-1, -2)
         return s1
 
-    def _load_inner(self, name, t, rows):
-        if name == "conv":
-            self.conv.copy_(t.reshape(-1, 1, self.k_inner)[rows])
-        elif name == "D" and self.D is not None:
-            self.D.copy_(t[rows])
-        else:
-            raise KeyError(f"unexpected tensor {name!r} for {type(self).__name__}")
 
 
 class HyenaIIRMixer(HyenaMixerBase):
@@ -463,12 +444,3 @@ class HyenaIIRMixer(HyenaMixerBase):
                                f"got {tuple(s2.shape[-2:])}")
         return s2
 
-    def _load_inner(self, name, t, rows):
-        if name == "log_poles":
-            self.log_poles.copy_(t.reshape(self.hidden_full, -1, 1)[rows])
-        elif name == "residues":
-            self.residues.copy_(t[rows])
-        elif name == "D":
-            self.D.copy_(t[rows])
-        else:
-            raise KeyError(f"unexpected tensor {name!r} for {type(self).__name__}")
