@@ -60,31 +60,13 @@ def embed_norm(tokens, table, device):
 
 
 def layer_params(kind, k, seed, device):
-    """BASELINE recipes: projections N(0, 0.02) (in_proj quantised to e4m3 with a
-    per-tensor scale), short filter N(0,1)/sqrt(3), FIR w[:, K-1-lag] =
-    N(0,1)/sqrt(K) exp(-0.05 lag), log-poles -exp(U(-6,0)), residues N(0,1)/16,
-    D N(0, 0.02), out_proj bias 0."""
-    g = torch.Generator().manual_seed(seed)
-    w_in = torch.randn(3 * H, H, generator=g) * 0.02
-    sw = w_in.abs().amax() / 448.0
-    p = {
-        "in_proj.weight": (w_in / sw).clamp(-448, 448).to(torch.float8_e4m3fn),
-        "in_proj.weight_scale": sw.reshape(1).float(),
-        "out_proj.weight": (torch.randn(H, H, generator=g) * 0.02).to(torch.bfloat16),
-        "out_proj.bias": torch.zeros(H, dtype=torch.bfloat16),
-        "short_filter": (torch.randn(3 * H, 1, 3, generator=g) / 3 ** 0.5).to(torch.bfloat16),
-    }
-    if kind == "hcl":
-        p["log_poles"] = -torch.exp(torch.rand(H, 16, 1, generator=g) * 6 - 6)
-        p["residues"] = torch.randn(H, 16, generator=g) / 16
-        p["D"] = (torch.randn(H, generator=g) * 0.02).to(torch.bfloat16)
-    else:
-        lag = torch.arange(k, dtype=torch.float32)
-        filt = torch.randn(H, k, generator=g) / k ** 0.5 * torch.exp(-0.05 * lag)
-        p["conv"] = filt.flip(-1).reshape(H, 1, k).to(torch.bfloat16)
-        if k >= 128:
-            p["D"] = (torch.randn(H, generator=g) * 0.02).to(torch.bfloat16)
-    return p
+    """BASELINE recipes (evo2_flash_b200.synthetic.mixer_tensors): projections
+    N(0, 0.02) with in_proj quantised to e4m3 under a per-tensor scale, short
+    filter N(0,1)/sqrt(3), FIR w[:, K-1-lag] = N(0,1)/sqrt(K) exp(-0.05 lag),
+    log-poles -exp(U(-6,0)), residues N(0,1)/16, D N(0, 0.02), out_proj bias 0."""
+    from evo2_flash_b200.synthetic import mixer_tensors
+
+    return mixer_tensors(kind, H, k, seed, fp8=True, device=device)
 
 
 TRIPLE = (("hcs", 7), ("hcm", 128), ("hcl", 16))

@@ -161,3 +161,39 @@ def decode_meta(slots, lengths=None, computed=None, device="cpu"):
 def meta_to(m, device):
     return SimpleNamespace(**{k: (v.to(device) if isinstance(v, torch.Tensor) else v)
                               for k, v in vars(m).items()})
+
+
+class OracleMixer(torch.nn.Module):
+    """A Hyena mixer computed by the CPU oracle, with the mixer-module surface the
+    model harness uses (load_full_weights, allocate_state, forward): the
+    all-reference arm of the full-model NLL comparison."""
+
+    def __init__(self, cfg, layer_idx, kind, k_inner, prefix, device="cpu"):
+        super().__init__()
+        self.kind, self.k_inner, self.H = kind, k_inner, cfg.hidden_size
+        self.p = None
+        self.states = None
+
+    def load_full_weights(self, t):
+        from oracle.hyena_oracle import MixerParams
+
+        t = {k: v.cpu() for k, v in t.items()}
+        fp8 = t["in_proj.weight"].dtype == torch.float8_e4m3fn
+        self.p = MixerParams(
+            H=self.H, kind="iir" if self.kind == "hcl" else "fir", k_inner=self.k_inner,
+            short_filter=t["short_filter"], conv=t.get("conv"), D=t.get("D"),
+            log_poles=t.get("log_poles"), residues=t.get("residues"),
+            in_proj_weight=t["in_proj.weight"],
+            in_proj_scales=(t["in_proj.input_scale"], t["in_proj.weight_scale"]) if fp8 else None,
+            out_proj_weight=t["out_proj.weight"], out_proj_bias=t["out_proj.bias"])
+
+    def allocate_state(self, num_blocks, device=None):
+        H = self.H
+        self.states = [torch.zeros(num_blocks, 2, 3 * H, dtype=torch.bfloat16),
+                       torch.zeros(num_blocks, 127, H), torch.zeros(num_blocks, H, 16)]
+
+    def forward(self, x, token_ids=None):
+        from evo2_flash_b200.forward_context import get_forward_metadata
+        from oracle.hyena_oracle import mixer_forward
+
+        return mixer_forward(x, self.p, get_forward_metadata(), self.states)
