@@ -15,6 +15,12 @@
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, scale / bias, bf16,
 //              16-byte global stores; the accumulator is handed back ("acc_empty")
 //              as soon as its last column is in registers
+// Small M (decode batches) cannot fill the SMs with output tiles, so K is split
+// across the CTAs of a thread-block cluster instead (gemm_cluster_kernel): each
+// CTA accumulates its K slice in TMEM, parks the fp32 partial in its own shared
+// memory, and after a cluster barrier every CTA sums a row slice of all the
+// partials over DSMEM in a fixed order (deterministic; no workspace, no atomics,
+// no second launch).
 // Every mbarrier wait is bounded by a globaltimer budget; on expiry the kernel
 // records the event in a device counter and runs to completion (TMEM freed).
 #include <cuda.h>
@@ -184,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
             const float* __restrict__ sa, const float* __restrict__ sb,
-            const bf16* __restrict__ bias, int splits, float* __restrict__ ws) {
+            const bf16* __restrict__ bias) {
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = Cfg<BN>::TMEM_COLS;
@@ -199,9 +205,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   // whole weight (<= 50 MB at the 7B shape) stays in L2 while the activations
   // stream through once.
   const int n_tiles = (N + BN - 1) / BN;
-  // Work units: (tile, K slice).  splits > 1 (small M only) sums the slices'
-  // fp32 partials into `ws`; a finalize kernel applies scale / bias.
-  const int total = n_tiles * ((M + BM - 1) / BM) * splits;
+  const int total = n_tiles * ((M + BM - 1) / BM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -238,11 +242,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const uint64_t pol_b = many_m ? policy_evict_last() : policy_evict_first();
       uint32_t it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
-        const int tile = unit / splits, sp = unit % splits;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
-        const int kb1 = (sp + 1) * kblocks / splits;
-        for (int kb = sp * kblocks / splits; kb < kb1; ++kb, ++it) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) { ok = false; break; }
           mbar_expect_tx(&S.full[s], STAGE_BYTES);
@@ -259,14 +261,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       constexpr uint32_t ID = idesc<FP8, BN>();
       uint32_t it = 0, ti = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++ti) {
-        const int sp = unit % splits;
-        const int kb0 = sp * kblocks / splits, kb1 = (sp + 1) * kblocks / splits;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++ti) {
         const int b = ti & 1;
         if (!mbar_wait(&S.acc_empty[b], ((ti >> 1) & 1) ^ 1)) ok = false;
         fence_after();
         const uint32_t d = tmem + uint32_t(b * BN);
-        for (int kb = kb0; kb < kb1 && ok; ++kb, ++it) {
+        for (int kb = 0; kb < kblocks && ok; ++kb, ++it) {
           const int s = it % STAGES;
           if (!mbar_wait(&S.full[s], (it / STAGES) & 1)) { ok = false; break; }
           fence_after();
@@ -274,7 +274,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           for (int kk = 0; kk < BKB / 32; ++kk) {
             const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
             const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
-            mma<FP8>(d, ad, bd, ID, (kb != kb0 || kk != 0) ? 1u : 0u);
+            mma<FP8>(d, ad, bd, ID, (kb != 0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&S.empty[s]);
         }
@@ -289,8 +289,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       scale_b = __ldg(sb);
     }
     uint32_t ti = 0;
-    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++ti) {
-      const int tile = unit / splits;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int b = ti & 1;
       const bool ok = mbar_wait(&S.acc_full[b], (ti >> 1) & 1);
@@ -308,18 +307,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         const int col0 = n0 + cb * 32;
         if (row >= M || col0 >= N) continue;
-        if (splits > 1) {  // K-slice partial: vector reduction into the fp32 workspace
-          float* wrow = ws + (long long)row * N + col0;
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            if (col0 + 4 * v >= N) break;
-            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + 4 * v),
-                         "f"(__uint_as_float(r[4 * v])), "f"(__uint_as_float(r[4 * v + 1])),
-                         "f"(__uint_as_float(r[4 * v + 2])), "f"(__uint_as_float(r[4 * v + 3]))
-                         : "memory");
-          }
-          continue;
-        }
         bf16* dst = out + (long long)row * ldo + col0;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
@@ -358,31 +345,222 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
 }
 
-// out = bf16((ws * sa) * sb) or bf16(ws + bias): the split-K epilogue.
-__global__ void __launch_bounds__(256)
-splitk_finalize_kernel(const float* __restrict__ ws, bf16* __restrict__ out, int64_t ldo, int M,
-                       int N, const float* __restrict__ sa, const float* __restrict__ sb,
-                       const bf16* __restrict__ bias) {
-  const int vpr = N / 4;
-  const long long total = (long long)M * vpr;
-  const float a = sa ? __ldg(sa) : 1.0f, b = sb ? __ldg(sb) : 1.0f;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / vpr;
-    const int c = int(i % vpr) * 4;
-    const float4 v = *reinterpret_cast<const float4*>(ws + row * N + c);
-    float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (sa) x[e] = (x[e] * a) * b;
-      if (bias) x[e] += __bfloat162float(bias[c + e]);
+// ---------------------------------------------------------------- small M
+// Shared memory of the cluster split-K kernel: the pipeline ring, reused after
+// the main loop as the CTA's fp32 partial tile (rows padded by 4 floats so the
+// 16-byte accesses of a warp fall in distinct banks).
+template <int BN>
+struct __align__(1024) SmemSK {
+  static constexpr int RED_LD = BN + 4;
+  static constexpr int RING = Cfg<BN>::STAGES * Cfg<BN>::STAGE_BYTES;
+  static constexpr int RED = BM * RED_LD * 4;
+  union {
+    struct {
+      uint8_t a[Cfg<BN>::STAGES][Cfg<BN>::A_BYTES];
+      uint8_t b[Cfg<BN>::STAGES][Cfg<BN>::B_BYTES];
+    } ring;
+    float red[BM][RED_LD];
+  } u;
+  uint64_t full[Cfg<BN>::STAGES];
+  uint64_t empty[Cfg<BN>::STAGES];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// One 128 x BN output tile per cluster of `splits` CTAs (grid (splits, tiles),
+// cluster (splits, 1, 1)); CTA r of the cluster accumulates K blocks
+// [r kblocks / splits, (r+1) kblocks / splits) and afterwards reduces rows
+// [r rows / splits, (r+1) rows / splits) of the tile over all CTAs' partials,
+// in rank order.  Warp roles as in gemm_kernel, one accumulator.
+template <bool FP8, int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, bf16* __restrict__ out, int64_t ldo,
+                    int M, int N, int K, const float* __restrict__ sa,
+                    const float* __restrict__ sb, const bf16* __restrict__ bias) {
+  constexpr int STAGES = Cfg<BN>::STAGES;
+  constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  constexpr int LD = SmemSK<BN>::RED_LD;
+  static_assert(SmemSK<BN>::RED <= SmemSK<BN>::RING, "partial tile must fit in the ring");
+  extern __shared__ uint8_t smem_raw[];
+  SmemSK<BN>& S = *reinterpret_cast<SmemSK<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                 ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int ELEM = FP8 ? 1 : 2;
+  constexpr int KE = BKB / ELEM;
+  const int kblocks = K / KE;
+  const int splits = (int)gridDim.x;
+  const int rank = (int)cluster_rank();
+  const int n_tiles = (N + BN - 1) / BN;
+  const int tile = (int)blockIdx.y;
+  const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+  const int kb0 = rank * kblocks / splits, kb1 = (rank + 1) * kblocks / splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
     }
-    const __nv_bfloat162 p = __floats2bfloat162_rn(x[0], x[1]);
-    const __nv_bfloat162 q = __floats2bfloat162_rn(x[2], x[3]);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&p);
-    o.y = *reinterpret_cast<const uint32_t*>(&q);
-    *reinterpret_cast<uint2*>(out + row * ldo + c) = o;
+    mbar_init(&S.acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&S.tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // The activations are re-read by every tile's cluster, the weights once.
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_first();
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) break;
+        mbar_expect_tx(&S.full[s], STAGE_BYTES);
+        tma_load_2d(&tmA, &S.full[s], S.u.ring.a[s], kb * KE, m0, pol_a);
+        tma_load_2d(&tmB, &S.full[s], S.u.ring.b[s], kb * KE, n0, pol_b);
+      }
+      // Drain: every issued copy has landed before the ring is reused.
+      for (int i = it > STAGES ? it - STAGES : 0; i < it; ++i)
+        mbar_wait(&S.full[i % STAGES], (i / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID = idesc<FP8, BN>();
+      int it = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&S.full[s], (it / STAGES) & 1)) break;
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKB / 32; ++kk) {
+          const uint64_t ad = sw128_desc(S.u.ring.a[s] + kk * 32);
+          const uint64_t bd = sw128_desc(S.u.ring.b[s] + kk * 32);
+          mma<FP8>(tmem, ad, bd, ID, (kb != kb0 || kk != 0) ? 1u : 0u);
+        }
+        mma_commit(&S.empty[s]);
+      }
+      mma_commit(&S.acc_full);  // fires once every MMA above has completed
+    }
+  }
+  // Epilogue warps wait for the accumulator; the whole CTA then meets, so the
+  // producer's drain is over and no copy can still land in the ring.
+  bool have = false;
+  if (warp >= 2) have = kb1 > kb0 && mbar_wait(&S.acc_full, 0);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp >= 2) {
+    // Partial tile: TMEM lane (row) 32 q + lane -> S.u.red[row][*].  An empty K
+    // slice contributes zeros.
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+#pragma unroll 1
+    for (int cb = 0; cb < BN / 32; ++cb) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      float4* dst = reinterpret_cast<float4*>(&S.u.red[row][cb * 32]);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+    }
+  }
+  __syncwarp();
+  fence_before();
+  cluster_sync_all();  // every CTA's partial tile is in its shared memory
+  fence_after();
+
+  // Reduction: rows [r0, r1) of the valid rows, 4 columns per thread per item.
+  {
+    const int rows = M - m0 < BM ? M - m0 : BM;
+    const int r0 = rank * rows / splits, r1 = (rank + 1) * rows / splits;
+    constexpr int GROUPS = BN / 4;
+    const int items = (r1 - r0) * GROUPS;
+    float scale = 1.0f, scale_b = 1.0f;
+    if constexpr (FP8) {
+      scale = __ldg(sa);
+      scale_b = __ldg(sb);
+    }
+    const uint32_t base = su32(&S.u.red[0][0]);
+    for (int i = threadIdx.x; i < items; i += THREADS) {
+      const int rr = r0 + i / GROUPS, c = (i % GROUPS) * 4;
+      const int col = n0 + c;
+      if (col >= N) continue;
+      const uint32_t off = uint32_t((rr * LD + c) * 4);
+      float4 acc = ld_cluster4(map_to_rank(base + off, 0));
+      for (int p = 1; p < splits; ++p) {
+        const float4 v = ld_cluster4(map_to_rank(base + off, (uint32_t)p));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      float x[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if constexpr (FP8) {
+          x[e] = (x[e] * scale) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+        } else {
+          if (bias != nullptr) x[e] += __bfloat162float(bias[col + e]);
+        }
+      }
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]);
+      const __nv_bfloat162 hi = __floats2bfloat162_rn(x[2], x[3]);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&lo);
+      o.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(out + (long long)(m0 + rr) * ldo + col) = o;
+    }
+  }
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while a partner still reads its partial
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS)
+                 : "memory");
   }
 }
 
@@ -432,7 +610,7 @@ static int num_sms() {
 template <bool FP8, int BN>
 static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* out, int64_t ldo,
                      int M, int N, int K, const float* sa, const float* sb, const void* bias,
-                     int splits, float* ws, cudaStream_t st) {
+                     cudaStream_t st) {
   CUtensorMap tb;
   int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
   if (rc) return rc;
@@ -444,51 +622,128 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
       return check_launch("cudaFuncSetAttribute(gemm)");
     attr = true;
   }
-  if (splits > 1 && cudaMemsetAsync(ws, 0, sizeof(float) * (size_t)M * N, st) != cudaSuccess)
-    return check_launch("cudaMemsetAsync(split-K workspace)");
-  const long long units = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM) * splits;
-  dim3 grid((unsigned)(units < num_sms() ? units : num_sms()));
+  const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  dim3 grid((unsigned)(tiles < num_sms() ? tiles : num_sms()));
   gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
-                                                    K, sa, sb, static_cast<const bf16*>(bias),
-                                                    splits, ws);
-  rc = check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
-  if (rc || splits == 1) return rc;
-  long long blocks = ((long long)M * (N / 4) + 255) / 256;
-  if (blocks > 4LL * num_sms()) blocks = 4LL * num_sms();
-  splitk_finalize_kernel<<<(unsigned)blocks, 256, 0, st>>>(ws, static_cast<bf16*>(out), ldo, M, N,
-                                                           sa, sb, static_cast<const bf16*>(bias));
-  return check_launch("splitk_finalize_kernel");
+                                                    K, sa, sb, static_cast<const bf16*>(bias));
+  return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
+}
+
+template <bool FP8, int BN>
+static size_t cluster_smem() {
+  return sizeof(SmemSK<BN>) + 1024;
+}
+
+template <bool FP8, int BN>
+static bool cluster_attr() {
+  static int state = 0;  // 0 unset, 1 ok, -1 failed
+  if (state == 0)
+    state = cudaFuncSetAttribute(gemm_cluster_kernel<FP8, BN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)cluster_smem<FP8, BN>()) == cudaSuccess ? 1 : -1;
+  return state > 0;
+}
+
+// How many clusters of `splits` CTAs can be resident at once (0 if unknown).
+template <bool FP8, int BN>
+static int resident_clusters(int splits) {
+  static int cache[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
+  if (splits < 1 || splits > 8) return 0;
+  if (cache[splits] < 0) {
+    int n = 0;
+    if (cluster_attr<FP8, BN>()) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)splits, 1, 1);
+      cfg.blockDim = dim3(THREADS, 1, 1);
+      cfg.dynamicSmemBytes = cluster_smem<FP8, BN>();
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = (unsigned)splits;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_cluster_kernel<FP8, BN>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    cache[splits] = n;
+  }
+  return cache[splits];
+}
+
+template <bool FP8, int BN>
+static int launch_cluster(const CUtensorMap& ta, const void* B, int64_t ldb, void* out,
+                          int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
+                          const void* bias, int splits, cudaStream_t st) {
+  CUtensorMap tb;
+  int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
+  if (rc) return rc;
+  if (!cluster_attr<FP8, BN>()) return check_launch("cudaFuncSetAttribute(gemm_cluster)");
+  const int tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)tiles, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = cluster_smem<FP8, BN>();
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<FP8, BN>, ta, tb, static_cast<bf16*>(out), ldo,
+                         M, N, K, sa, sb, static_cast<const bf16*>(bias)) != cudaSuccess)
+    return check_launch(FP8 ? "gemm_cluster_kernel<e4m3>" : "gemm_cluster_kernel<bf16>");
+  return check_launch(FP8 ? "gemm_cluster_kernel<e4m3>" : "gemm_cluster_kernel<bf16>");
 }
 
 struct Plan {
-  int bn, splits;
+  int bn, splits;  // splits > 1: cluster split-K kernel
 };
 
-static bool mt_cover(int M, int N) {
-  return (long long)((M + BM - 1) / BM) * ((N + 63) / 64) >= num_sms();
+template <bool FP8>
+static int resident(int bn, int splits) {
+  return bn == 256 ? resident_clusters<FP8, 256>(splits) : resident_clusters<FP8, 128>(splits);
 }
 
-// Large M: the widest N-tile that still gives every SM a tile, unsplit.
-// Small M (decode batches): 256-wide tiles with K split so that tiles x slices
-// cover the SMs once, each slice at least two K stages long.
-static Plan plan(int M, int N, int K, bool fp8) {
+// Large M: the widest N-tile that still gives every SM a tile (persistent
+// kernel).  Small M (decode batches): split K over a cluster of 2-8 CTAs per
+// 128 x BN tile, choosing the (BN, splits) that puts the most CTAs to work in one
+// resident wave (ties: fewer splits, i.e. less reduction traffic), each slice
+// at least two K stages long.  Otherwise narrow tiles, unsplit.
+template <bool FP8>
+static Plan plan(int M, int N, int K) {
   const long long mt = (M + BM - 1) / BM;
   const int sms = num_sms();
   for (int bn : {256, 128}) {
     if (mt * ((N + bn - 1) / bn) >= sms) return {bn, 1};
   }
-  const int kblocks = K / (BKB / (fp8 ? 1 : 2));
-  const long long tiles = mt * ((N + 255) / 256);
-  long long sp = sms / tiles;
-  if (sp > kblocks / 2) sp = kblocks / 2;
-  if (sp >= 2 && N % 4 == 0) return {256, (int)sp};
+  const int kblocks = K / (BKB / (FP8 ? 1 : 2));
+  Plan best = {0, 0};
+  long long best_ctas = 0;
+  for (int bn : {256, 128}) {
+    const long long tiles = mt * ((N + bn - 1) / bn);
+    for (int sp = 2; sp <= 8; ++sp) {
+      if (kblocks / sp < 2 || tiles * sp > sms) break;
+      if (resident<FP8>(bn, sp) < tiles) continue;
+      const long long ctas = tiles * sp;
+      if (ctas > best_ctas || (ctas == best_ctas && sp < best.splits)) {
+        best = {bn, sp};
+        best_ctas = ctas;
+      }
+    }
+  }
+  if (best.splits > 1) return best;
   return {mt * ((N + 63) / 64) >= sms ? 64 : 32, 1};
 }
 
 template <bool FP8>
 static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out, int64_t ldo,
                   int M, int N, int K, const float* sa, const float* sb, const void* bias,
-                  void* ws, size_t ws_bytes, cudaStream_t st) {
+                  cudaStream_t st) {
   if (M <= 0 || N <= 0) return HYENA_OK;
   const int KE = BKB / (FP8 ? 1 : 2);
   HB_REQUIRE(K > 0 && K % KE == 0, FP8 ? "e4m3 GEMM needs K % 128 == 0" : "bf16 GEMM needs K % 64 == 0");
@@ -500,36 +755,46 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   CUtensorMap ta;
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
-  Plan pl = plan(M, N, K, FP8);
-  if (pl.splits > 1 && (ws == nullptr || ws_bytes < sizeof(float) * (size_t)M * N || !aligned16(ws)))
-    pl = {mt_cover(M, N) ? 64 : 32, 1};
-  float* w = static_cast<float*>(ws);
+  const Plan pl = plan<FP8>(M, N, K);
+  if (pl.splits > 1) {
+    if (pl.bn == 256)
+      return launch_cluster<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+    return launch_cluster<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+  }
   switch (pl.bn) {
-    case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, w, st);
-    case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
-    case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
-    default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, 1, w, st);
+    case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
   }
 }
 
 }  // namespace gemm
 
+// `ws` / `ws_bytes` are accepted for ABI stability and not used: small-M
+// calls reduce their K slices inside a cluster.
 int gemm_e4m3_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                      int64_t ldo, int M, int N, int K, const float* sa, const float* sb,
                      void* ws, size_t ws_bytes, cudaStream_t st) {
-  return gemm::launch<true>(A, lda, B, ldb, out, ldo, M, N, K, sa, sb, nullptr, ws, ws_bytes, st);
+  (void)ws;
+  (void)ws_bytes;
+  return gemm::launch<true>(A, lda, B, ldb, out, ldo, M, N, K, sa, sb, nullptr, st);
 }
 
 int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
                      int64_t ldo, int M, int N, int K, const void* bias, void* ws,
                      size_t ws_bytes, cudaStream_t st) {
-  return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, ws,
-                             ws_bytes, st);
+  (void)ws;
+  (void)ws_bytes;
+  return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, st);
 }
 
 size_t gemm_workspace_size(int M, int N, int K, bool fp8) {
-  const gemm::Plan p = gemm::plan(M, N, K, fp8);
-  return p.splits > 1 ? sizeof(float) * (size_t)M * N : 0;
+  (void)M;
+  (void)N;
+  (void)K;
+  (void)fp8;
+  return 0;
 }
 
 }  // namespace hb

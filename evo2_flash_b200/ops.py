@@ -265,7 +265,8 @@ def gemm_e4m3(a, b, scale_a, scale_b, out=None):
 
 
 def _gemm_workspace(lib, M, N, K, fp8, device):
-    """fp32 split-K workspace for small-M GEMMs (torch caching allocator)."""
+    """Workspace the library asks for at this shape (none at present: small-M
+    GEMMs reduce their K slices inside a thread-block cluster)."""
     n = lib.hyena_gemm_workspace_size(M, N, K, int(fp8))
     return torch.empty(n // 4, dtype=torch.float32, device=device) if n else None
 

@@ -174,8 +174,9 @@ HYENA_API int hyena_quant_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq,
  * the in_proj GEMM (mixers.py:1076-1092 -> vLLM Fp8 ReplicatedLinear; numerics
  * contract fp8_emul.py:81-88 with fp32 accumulation).  tcgen05 + TMA + TMEM.
  * Requires K % 128 == 0, N % 8 == 0, 16-byte aligned rows.
- * `workspace` (fp32, hyena_gemm_workspace_size bytes, may be NULL) lets small-M
- * calls (decode batches) split K across SMs; without it they run unsplit. */
+ * Small-M calls (decode batches) split K over the CTAs of a thread-block cluster
+ * and reduce the slices in shared memory; `workspace` / `workspace_bytes` are
+ * accepted for ABI stability and ignored (pass NULL, 0). */
 HYENA_API int hyena_gemm_e4m3(const void* A, int64_t lda, const void* B, int64_t ldb,
                     void* out, int64_t ldo, int32_t M, int32_t N, int32_t K,
                     const float* scale_a, const float* scale_b, void* workspace,
@@ -183,14 +184,15 @@ HYENA_API int hyena_gemm_e4m3(const void* A, int64_t lda, const void* B, int64_t
 
 /* out(M,N) bf16 = A(M,K) bf16 . B(N,K) bf16^T [+ bias(N)]: the out_proj GEMM
  * (mixers.py:801-803, 1304, 1400 -> ReplicatedLinear with bias). tcgen05 + TMA.
- * Requires K % 64 == 0, N % 8 == 0, 16-byte aligned rows.  Workspace as above. */
+ * Requires K % 64 == 0, N % 8 == 0, 16-byte aligned rows.  Workspace ignored,
+ * as above. */
 HYENA_API int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
                     void* out, int64_t ldo, int32_t M, int32_t N, int32_t K,
                     const void* bias, void* workspace, size_t workspace_bytes,
                     void* stream);
 
-/* Bytes of fp32 workspace the GEMMs above use for split-K at this shape (0 when
- * the shape runs unsplit).  fp8 != 0 selects the e4m3 GEMM. */
+/* Bytes of workspace the GEMMs above use at this shape: always 0 (kept so that
+ * callers written against ABI version 2 keep working).  fp8 != 0 selects e4m3. */
 HYENA_API size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8);
 
 /* ---------------------------------------------------------------- misc */
