@@ -177,6 +177,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The same load without the wait, so that several can be in flight.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // Instruction descriptor: fp32 accumulator, K-major A and B, M=128, N=256;
 // operand format E4M3 (kind::f8f6f4) or BF16 (kind::f16).
 template <bool FP8, int BN>
@@ -346,24 +364,42 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 }
 
 // ---------------------------------------------------------------- small M
-// Shared memory of the cluster split-K kernel: the pipeline ring, reused after
-// the main loop as the CTA's fp32 partial tile (rows padded by 4 floats so the
-// 16-byte accesses of a warp fall in distinct banks).
+// Shared memory of the cluster split-K kernel.  After the main loop the ring
+// is reused as
+//   staging  [BM][LD]            this CTA's fp32 partial, rows other CTAs own
+//   inbox    [splits-1][R][LD]   the other ranks' partials of the rows this CTA
+//                                owns (slots in rank order, skipping itself)
+// with R = ceil(BM / splits) and rows padded to LD = BN + 4 floats, so that a
+// warp's 16-byte accesses to 32 consecutive rows fall in distinct banks.
+template <int BN>
+constexpr int max_cluster_splits() {
+  return BN >= 256 ? 3 : 4;
+}
+constexpr int max_inbox_rows(int ms) {  // max over splits 2..ms of (splits-1) ceil(BM/splits)
+  int best = 0;
+  for (int sp = 2; sp <= ms; ++sp) {
+    const int r = (sp - 1) * ((BM + sp - 1) / sp);
+    best = r > best ? r : best;
+  }
+  return best;
+}
 template <int BN>
 struct __align__(1024) SmemSK {
   static constexpr int RED_LD = BN + 4;
-  static constexpr int RING = Cfg<BN>::STAGES * Cfg<BN>::STAGE_BYTES;
-  static constexpr int RED = BM * RED_LD * 4;
+  static constexpr int INBOX_ROWS = max_inbox_rows(max_cluster_splits<BN>());
+  static constexpr int RED_ROWS = BM + INBOX_ROWS;
   union {
     struct {
       uint8_t a[Cfg<BN>::STAGES][Cfg<BN>::A_BYTES];
       uint8_t b[Cfg<BN>::STAGES][Cfg<BN>::B_BYTES];
     } ring;
-    float red[BM][RED_LD];
+    float red[RED_ROWS * RED_LD];
   } u;
   uint64_t full[Cfg<BN>::STAGES];
   uint64_t empty[Cfg<BN>::STAGES];
   uint64_t acc_full;
+  uint64_t inbox_full;
+  float bias_s[BN];
   uint32_t tmem_base;
 };
 
@@ -381,20 +417,42 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
+__device__ __forceinline__ void st_cluster4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                            uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
                : "memory");
-  return v;
+}
+// Bulk copy of `bytes` from this CTA's shared memory into another CTA's
+// (cluster address), completing `bytes` of transaction count on that CTA's
+// mbarrier (cluster address).
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes,
+                                                     uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void epilogue_bar() {  // the four epilogue warps only
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+template <int N>
+__host__ __device__ constexpr uint32_t pow2_cols() {
+  return N <= 32 ? 32u : N <= 64 ? 64u : N <= 128 ? 128u : N <= 256 ? 256u : 512u;
 }
 
 // One 128 x BN output tile per cluster of `splits` CTAs (grid (splits, tiles),
-// cluster (splits, 1, 1)); CTA r of the cluster accumulates K blocks
-// [r kblocks / splits, (r+1) kblocks / splits) and afterwards reduces rows
-// [r rows / splits, (r+1) rows / splits) of the tile over all CTAs' partials,
-// in rank order.  Warp roles as in gemm_kernel, one accumulator.
+// cluster (splits, 1, 1); splits = 1 is a plain one-tile-per-CTA GEMM).  CTA r
+// accumulates K blocks [r kblocks / splits, (r+1) kblocks / splits) in TMEM and
+// owns rows [r R, (r+1) R) of the tile.  After a cluster barrier (every ring is
+// idle) each CTA stages the rows other CTAs own in its shared memory and sends
+// each owner its rows with one bulk copy; every owner waits for its inbox on an
+// mbarrier, sums all ranks' partials in rank order (its own straight from TMEM;
+// deterministic), scales / adds bias and stores bf16.  A last cluster barrier
+// keeps every staging area alive until all copies have landed.
 template <bool FP8, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -403,9 +461,9 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
                     const float* __restrict__ sb, const bf16* __restrict__ bias) {
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
-  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  constexpr uint32_t TMEM_COLS = pow2_cols<BN>();
   constexpr int LD = SmemSK<BN>::RED_LD;
-  static_assert(SmemSK<BN>::RED <= SmemSK<BN>::RING, "partial tile must fit in the ring");
+  static_assert(BN % 32 == 0, "epilogue reads 32 columns at a time");
   extern __shared__ uint8_t smem_raw[];
   SmemSK<BN>& S = *reinterpret_cast<SmemSK<BN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                  ~uintptr_t(1023));
@@ -415,10 +473,21 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
   const int kblocks = K / KE;
   const int splits = (int)gridDim.x;
   const int rank = (int)cluster_rank();
+  const int rows_per = (BM + splits - 1) / splits;
   const int n_tiles = (N + BN - 1) / BN;
   const int tile = (int)blockIdx.y;
   const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
   const int kb0 = rank * kblocks / splits, kb1 = (rank + 1) * kblocks / splits;
+  const int rows = M - m0 < BM ? M - m0 : BM;  // valid rows of the tile
+  // Rows [o R, o R + owned(o)) belong to rank o.
+  auto owned = [&](int o) {
+    const int lo = o * rows_per, hi = (o + 1) * rows_per < rows ? (o + 1) * rows_per : rows;
+    return hi > lo ? hi - lo : 0;
+  };
+  const int my_rows = owned(rank);
+  const uint32_t inbox_bytes = uint32_t((splits - 1) * my_rows * LD * 4);
+  float* staging = S.u.red;
+  float* inbox = S.u.red + BM * LD;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -426,7 +495,9 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
       mbar_init(&S.empty[s], 1);
     }
     mbar_init(&S.acc_full, 1);
+    mbar_init(&S.inbox_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(&S.inbox_full, inbox_bytes);  // the one arrival; the copies bring the bytes
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
@@ -478,85 +549,158 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
       mma_commit(&S.acc_full);  // fires once every MMA above has completed
     }
   }
-  // Epilogue warps wait for the accumulator; the whole CTA then meets, so the
-  // producer's drain is over and no copy can still land in the ring.
   bool have = false;
-  if (warp >= 2) have = kb1 > kb0 && mbar_wait(&S.acc_full, 0);
-  fence_before();
-  __syncthreads();
-  fence_after();
+  float scale = 1.0f, scale_b = 1.0f;
   if (warp >= 2) {
-    // Partial tile: TMEM lane (row) 32 q + lane -> S.u.red[row][*].  An empty K
-    // slice contributes zeros.
-    const int q = warp & 3;
-    const int row = 32 * q + lane;
-#pragma unroll 1
-    for (int cb = 0; cb < BN / 32; ++cb) {
-      uint32_t r[32];
-      if (have) {
-        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
-      }
-      float4* dst = reinterpret_cast<float4*>(&S.u.red[row][cb * 32]);
-#pragma unroll
-      for (int v = 0; v < 8; ++v)
-        dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-    }
-  }
-  __syncwarp();
-  fence_before();
-  cluster_sync_all();  // every CTA's partial tile is in its shared memory
-  fence_after();
-
-  // Reduction: rows [r0, r1) of the valid rows, 4 columns per thread per item.
-  {
-    const int rows = M - m0 < BM ? M - m0 : BM;
-    const int r0 = rank * rows / splits, r1 = (rank + 1) * rows / splits;
-    constexpr int GROUPS = BN / 4;
-    const int items = (r1 - r0) * GROUPS;
-    float scale = 1.0f, scale_b = 1.0f;
+    // While the main loop runs: epilogue constants into registers / shared memory.
     if constexpr (FP8) {
       scale = __ldg(sa);
       scale_b = __ldg(sb);
+    } else {
+      for (int j = threadIdx.x - 64; j < BN; j += 128)
+        S.bias_s[j] = (bias != nullptr && n0 + j < N) ? __bfloat162float(bias[n0 + j]) : 0.0f;
     }
-    const uint32_t base = su32(&S.u.red[0][0]);
-    for (int i = threadIdx.x; i < items; i += THREADS) {
-      const int rr = r0 + i / GROUPS, c = (i % GROUPS) * 4;
-      const int col = n0 + c;
-      if (col >= N) continue;
-      const uint32_t off = uint32_t((rr * LD + c) * 4);
-      float4 acc = ld_cluster4(map_to_rank(base + off, 0));
-      for (int p = 1; p < splits; ++p) {
-        const float4 v = ld_cluster4(map_to_rank(base + off, (uint32_t)p));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      float x[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if constexpr (FP8) {
-          x[e] = (x[e] * scale) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+    have = __all_sync(0xffffffffu, kb1 > kb0 && mbar_wait(&S.acc_full, 0));
+  }
+  // Barrier 1: in every CTA of the cluster the main loop is over (producer
+  // drained, accumulator complete), so every ring may now be staging / inbox.
+  fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  fence_after();
+
+  const int q = warp & 3;  // TMEM lane quarter of an epilogue warp
+  const int row = 32 * q + lane;
+  const int owner = row / rows_per;
+  if (warp >= 2) {
+    // Stage the rows other ranks own (an empty K slice stages zeros).
+    const bool stage = owner != rank && row < rows;
+    if (__any_sync(0xffffffffu, stage)) {
+      float4* dst = reinterpret_cast<float4*>(staging + row * LD);
+#pragma unroll 1
+      for (int cb = 0; cb < BN / 32; cb += 2) {
+        uint32_t r[2][32];
+        if (have) {
+          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r[0]);
+          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32 + 32), r[1]);
+          tmem_wait_ld();
         } else {
-          if (bias != nullptr) x[e] += __bfloat162float(bias[col + e]);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[0][j] = r[1][j] = 0u;
+        }
+        if (stage) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[(cb + h) * 8 + v] =
+                  make_float4(__uint_as_float(r[h][4 * v]), __uint_as_float(r[h][4 * v + 1]),
+                              __uint_as_float(r[h][4 * v + 2]), __uint_as_float(r[h][4 * v + 3]));
         }
       }
-      const __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]);
-      const __nv_bfloat162 hi = __floats2bfloat162_rn(x[2], x[3]);
-      uint2 o;
-      o.x = *reinterpret_cast<const uint32_t*>(&lo);
-      o.y = *reinterpret_cast<const uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(out + (long long)(m0 + rr) * ldo + col) = o;
+    }
+    fence_proxy_async_smem();  // staged rows -> visible to the bulk-copy engine
+    epilogue_bar();
+    if (threadIdx.x == 64) {
+      for (int o = 0; o < splits; ++o) {
+        const int n = owned(o);
+        if (o == rank || n == 0) continue;
+        const int slot = rank < o ? rank : rank - 1;
+        const uint32_t dst =
+            map_to_rank(su32(inbox + slot * rows_per * LD), (uint32_t)o);
+        const uint32_t bar = map_to_rank(su32(&S.inbox_full), (uint32_t)o);
+        bulk_copy_to_cluster(dst, su32(staging + o * rows_per * LD), uint32_t(n * LD * 4), bar);
+      }
+    }
+    // Reduce own rows: all ranks' partials in rank order, this rank's from TMEM.
+    const bool mine = owner == rank && row < rows;
+    if (__any_sync(0xffffffffu, mine)) {
+      const bool ready = inbox_bytes == 0 || mbar_wait(&S.inbox_full, 0);
+      const int lr = row - rank * rows_per;
+      // This row's own scratch for its bf16 result (inbox slot 0, read up to
+      // the column written; the staging row when nothing is inboxed), stored
+      // coalesced below.
+      uint4* rowbuf = reinterpret_cast<uint4*>(splits > 1 ? inbox + lr * LD : staging + row * LD);
+#pragma unroll 1
+      for (int cb = 0; cb < BN / 32; cb += 2) {
+        uint32_t r[2][32];
+        if (have) {
+          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r[0]);
+          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32 + 32), r[1]);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[0][j] = r[1][j] = 0u;
+        }
+        if (!mine || !ready) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c0 = (cb + h) * 32;
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
+          for (int p = 0; p < splits; ++p) {
+            if (p == rank) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(r[h][j]);
+            } else {
+              const int slot = p < rank ? p : p - 1;
+              const float4* src =
+                  reinterpret_cast<const float4*>(inbox + (slot * rows_per + lr) * LD + c0);
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                const float4 x = src[v];
+                acc[4 * v] += x.x;
+                acc[4 * v + 1] += x.y;
+                acc[4 * v + 2] += x.z;
+                acc[4 * v + 3] += x.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 pk;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float x0 = acc[8 * v + 2 * e], x1 = acc[8 * v + 2 * e + 1];
+              if constexpr (FP8) {
+                x0 = (x0 * scale) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+                x1 = (x1 * scale) * scale_b;
+              } else {
+                x0 += S.bias_s[c0 + 8 * v + 2 * e];
+                x1 += S.bias_s[c0 + 8 * v + 2 * e + 1];
+              }
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+              pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            rowbuf[(cb + h) * 4 + v] = pk;
+          }
+        }
+      }
+    }
+    // Coalesced store of the owned rows: one row per warp step, 16 bytes a lane.
+    epilogue_bar();
+    {
+      constexpr int VPR = BN / 8;  // 16-byte vectors per row
+      const int ew = warp - 2;
+      for (int lr = ew; lr < my_rows; lr += 4) {
+        const int rrow = rank * rows_per + lr;
+        const uint4* rowbuf = reinterpret_cast<const uint4*>(
+            splits > 1 ? inbox + lr * LD : staging + rrow * LD);
+        bf16* dst = out + (long long)(m0 + rrow) * ldo + n0;
+        for (int v = lane; v < VPR; v += 32) {
+          if (n0 + 8 * v < N) *reinterpret_cast<uint4*>(dst + 8 * v) = rowbuf[v];
+        }
+      }
     }
   }
+  // Barrier 2: every bulk copy has landed (each owner waited for its inbox),
+  // so no staging area is still being read when its CTA exits.
+  fence_before();
   __syncwarp();
-  cluster_sync_all();  // no CTA leaves while a partner still reads its partial
+  cluster_sync_all();
   if (warp == 1) {
-    __syncwarp();
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS)
@@ -701,43 +845,50 @@ static int launch_cluster(const CUtensorMap& ta, const void* B, int64_t ldb, voi
 }
 
 struct Plan {
-  int bn, splits;  // splits > 1: cluster split-K kernel
+  int bn, splits;  // splits > 0: cluster kernel with that many K slices per tile
 };
 
 template <bool FP8>
 static int resident(int bn, int splits) {
-  return bn == 256 ? resident_clusters<FP8, 256>(splits) : resident_clusters<FP8, 128>(splits);
+  switch (bn) {
+    case 256: return resident_clusters<FP8, 256>(splits);
+    case 192: return resident_clusters<FP8, 192>(splits);
+    case 128: return resident_clusters<FP8, 128>(splits);
+    default: return resident_clusters<FP8, 64>(splits);
+  }
 }
 
 // Large M: the widest N-tile that still gives every SM a tile (persistent
-// kernel).  Small M (decode batches): split K over a cluster of 2-8 CTAs per
-// 128 x BN tile, choosing the (BN, splits) that puts the most CTAs to work in one
-// resident wave (ties: fewer splits, i.e. less reduction traffic), each slice
-// at least two K stages long.  Otherwise narrow tiles, unsplit.
+// kernel, splits = 0).  Small M (decode batches): the cluster kernel with the
+// (BN, splits) that, in one resident wave of at most one CTA per SM, puts the
+// fewest operand bytes through any one SM ((BM + BN) x its K slice; ties: fewer
+// splits), each K slice at least two stages long.
 template <bool FP8>
 static Plan plan(int M, int N, int K) {
   const long long mt = (M + BM - 1) / BM;
   const int sms = num_sms();
   for (int bn : {256, 128}) {
-    if (mt * ((N + bn - 1) / bn) >= sms) return {bn, 1};
+    if (mt * ((N + bn - 1) / bn) >= sms) return {bn, 0};
   }
   const int kblocks = K / (BKB / (FP8 ? 1 : 2));
   Plan best = {0, 0};
-  long long best_ctas = 0;
-  for (int bn : {256, 128}) {
+  long long best_cost = 0;
+  for (int bn : {256, 192, 128, 64}) {
     const long long tiles = mt * ((N + bn - 1) / bn);
-    for (int sp = 2; sp <= 8; ++sp) {
-      if (kblocks / sp < 2 || tiles * sp > sms) break;
+    for (int sp = 1; sp <= 8; ++sp) {
+      if (tiles * sp > sms || sp > (bn >= 256 ? max_cluster_splits<256>() : max_cluster_splits<128>()))
+        break;
+      if (sp > 1 && kblocks / sp < 2) break;
       if (resident<FP8>(bn, sp) < tiles) continue;
-      const long long ctas = tiles * sp;
-      if (ctas > best_ctas || (ctas == best_ctas && sp < best.splits)) {
+      const long long cost = (long long)(BM + bn) * ((kblocks + sp - 1) / sp);
+      if (best.splits == 0 || cost < best_cost || (cost == best_cost && sp < best.splits)) {
         best = {bn, sp};
-        best_ctas = ctas;
+        best_cost = cost;
       }
     }
   }
-  if (best.splits > 1) return best;
-  return {mt * ((N + 63) / 64) >= sms ? 64 : 32, 1};
+  if (best.splits > 0) return best;
+  return {mt * ((N + 63) / 64) >= sms ? 64 : 32, 0};
 }
 
 template <bool FP8>
@@ -756,10 +907,17 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
   const Plan pl = plan<FP8>(M, N, K);
-  if (pl.splits > 1) {
-    if (pl.bn == 256)
-      return launch_cluster<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
-    return launch_cluster<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+  if (pl.splits > 0) {
+    switch (pl.bn) {
+      case 256:
+        return launch_cluster<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+      case 192:
+        return launch_cluster<FP8, 192>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+      case 128:
+        return launch_cluster<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+      default:
+        return launch_cluster<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, pl.splits, st);
+    }
   }
   switch (pl.bn) {
     case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
