@@ -25,6 +25,51 @@ int check_launch(const char* what);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---------------------------------------------------------------- launches
+// Every kernel of the library is launched with programmatic dependent launch,
+// so that it can be scheduled while the previous kernel in the stream drains.
+// A kernel first lets its own successor launch (pdl_trigger: the successor's
+// CTAs start once every CTA of this grid has started) and then, in every
+// thread, calls pdl_wait() before its first load or store of global memory
+// that other kernels write or read; only shared-memory / TMEM set-up and
+// tensor-map or L2 prefetches may precede that wait.  Without a programmatic
+// predecessor pdl_wait() returns at once.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+  pdl_trigger();
+  pdl_wait();
+}
+
+// cudaLaunchKernelEx with the programmatic-serialisation attribute (and a
+// 1-D cluster of `cluster_x` CTAs when cluster_x > 0).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  unsigned n = 0;
+  at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 0) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster_x;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 // ---------------------------------------------------------------- device math
 // Round to bf16 and back: the value a torch op with a bf16 output stores.
 __device__ __forceinline__ float bf16r(float x) {

@@ -42,6 +42,7 @@ __device__ __forceinline__ bool block_ok(long long b, const hyena_state_view& v)
 template <int KIND, int K>
 __global__ void __launch_bounds__(DEC_THREADS)
 decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  pdl_entry();
   const int r = blockIdx.x;
   const int h = blockIdx.y * DEC_THREADS + threadIdx.x;
   if (h >= P.H) return;
@@ -245,48 +246,62 @@ __device__ __forceinline__ void store_bf16x4(bf16* p, const float (&v)[4]) {
   *reinterpret_cast<uint2*>(p) = r;
 }
 
-// Short filter + gate for `C` consecutive channels starting at h: reads the
-// triple row of z and window columns 0, 1 of S0 (block cin), writes [c1, x] to
-// block cout.  Returns x2 and u per channel.
+// Short filter + gate for `C` consecutive channels starting at h, in two
+// halves so that callers can put its loads in flight together with their own:
+// gate_load reads the triple row of z, window columns 0, 1 of S0 (block cin)
+// and the short taps; gate_finish computes x2 and u per channel and writes
+// [c1, x] to block cout.
 template <int C>
-__device__ __forceinline__ void short_gate_q1(const hyena_layer_params& P,
-                                              const hyena_decode_args& A, int t0, int h,
-                                              long long cin, long long cout, bool write_conv,
-                                              float (&x2)[C], float (&u)[C]) {
+struct GateIn {
+  float zx[3 * C], w0[3 * C], w1[3 * C];
+  uint2 swr[9 * C / 4];  // short taps of the C channels: 9C contiguous bf16
+};
+
+template <int C>
+__device__ __forceinline__ void gate_load(const hyena_layer_params& P, const hyena_decode_args& A,
+                                          int t0, int h, long long cin, GateIn<C>& g) {
+  static_assert(C % 4 == 0, "vector path: 4-channel multiples");
   const bf16* z = static_cast<const bf16*>(A.z) + (long long)t0 * A.ldz + 3 * h;
-  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const bf16* s0 = static_cast<const bf16*>(A.conv_state.data);
   const bf16* c0p = s0 + cin * A.conv_state.block_stride + 3 * h;
   const bf16* c1p = c0p + A.conv_state.col_stride;
-  // short taps of the C channels: 9C contiguous bf16, 8-byte aligned for C % 4 == 0
   const uint2* swv = reinterpret_cast<const uint2*>(static_cast<const bf16*>(P.short_w) + 9 * h);
-  uint2 swr[9 * C / 4];
 #pragma unroll
-  for (int i = 0; i < 9 * C / 4; ++i) swr[i] = __ldg(swv + i);
-  const bf16* sw = reinterpret_cast<const bf16*>(swr);
-  float zx[3 * C], w0[3 * C], w1[3 * C];
+  for (int i = 0; i < 9 * C / 4; ++i) g.swr[i] = __ldg(swv + i);
 #pragma unroll
   for (int i = 0; i < 3 * C; i += 4) {
     float a[4], b[4];
     load_bf16x4(z + i, a);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) zx[i + k] = a[k];
+    for (int k = 0; k < 4; ++k) g.zx[i + k] = a[k];
     load_bf16x4(c0p + i, a);
     load_bf16x4(c1p + i, b);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) { w0[i + k] = a[k]; w1[i + k] = b[k]; }
+    for (int k = 0; k < 4; ++k) {
+      g.w0[i + k] = a[k];
+      g.w1[i + k] = b[k];
+    }
   }
+}
+
+template <int C>
+__device__ __forceinline__ void gate_finish(const hyena_decode_args& A, int h, long long cout,
+                                            bool write_conv, const GateIn<C>& g, float (&x2)[C],
+                                            float (&u)[C]) {
+  const bf16* sw = reinterpret_cast<const bf16*>(g.swr);
   float o[3 * C];
 #pragma unroll
   for (int i = 0; i < 3 * C; ++i)
-    o[i] = short_tap(w0[i], w1[i], zx[i], __bfloat162float(sw[3 * i]),
+    o[i] = short_tap(g.w0[i], g.w1[i], g.zx[i], __bfloat162float(sw[3 * i]),
                      __bfloat162float(sw[3 * i + 1]), __bfloat162float(sw[3 * i + 2]));
   if (write_conv) {
+    bf16* s0 = static_cast<bf16*>(A.conv_state.data);
     bf16* d0 = s0 + cout * A.conv_state.block_stride + 3 * h;
     bf16* d1 = d0 + A.conv_state.col_stride;
 #pragma unroll
     for (int i = 0; i < 3 * C; i += 4) {
-      float a[4] = {w1[i], w1[i + 1], w1[i + 2], w1[i + 3]};
-      float b[4] = {zx[i], zx[i + 1], zx[i + 2], zx[i + 3]};
+      float a[4] = {g.w1[i], g.w1[i + 1], g.w1[i + 2], g.w1[i + 3]};
+      float b[4] = {g.zx[i], g.zx[i + 1], g.zx[i + 2], g.zx[i + 3]};
       store_bf16x4(d0 + i, a);
       store_bf16x4(d1 + i, b);
     }
@@ -301,13 +316,17 @@ __device__ __forceinline__ void short_gate_q1(const hyena_layer_params& P,
 template <int K>
 __global__ void __launch_bounds__(FAST_THREADS)
 decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  pdl_entry();
   constexpr int HIST = K - 1;
   constexpr int U = 8;  // taps in flight
   const int r = blockIdx.x;
   const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
   if (h >= P.H) return;
+  // Routing first, all four loads in flight at once.
   const long long cin = __ldg(A.conv_in_block + r);
   const long long cout = __ldg(A.conv_out_block + r);
+  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
+  const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
   bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo + h;
   if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
     if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
@@ -318,11 +337,12 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   }
   const bool write_conv = block_ok(cout, A.conv_state) &&
                           !(A.skip_null_writes && cout == A.null_block);
+  // The gate's inputs are loaded now; for the long window they are consumed
+  // after the window stream, so that both sets of loads are in flight at once.
+  GateIn<4> gin;
+  gate_load<4>(P, A, r, h, cin, gin);
   float x2[4], u[4];
-  short_gate_q1<4>(P, A, r, h, cin, cout, write_conv, x2, u);
-
-  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
-  const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
+  if constexpr (HIST < 32) gate_finish<4>(A, h, cout, write_conv, gin, x2, u);  // short window
   const bool src_ok = block_ok(src, A.inner_state);
   const bool dok = block_ok(dst, A.inner_state) && !(A.skip_null_writes && dst == A.null_block);
   if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
@@ -358,6 +378,7 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
       }
     }
   }
+  if constexpr (HIST >= 32) gate_finish<4>(A, h, cout, write_conv, gin, x2, u);
   float wl[4];
   load_bf16x4(w + (long long)HIST * wk, wl);
 #pragma unroll
@@ -376,70 +397,131 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   store_bf16x4(out, g);
 }
 
-__global__ void __launch_bounds__(FAST_THREADS)
+// LI q = 1 decode.  A block covers 64 channels of IIR_R requests in two
+// phases.  Gate phase: one thread per (request, 4 channels) runs the short
+// filter + gate (4-wide vector path, S0 window written) into shared memory.
+// State phase: four threads per channel, each owning four of its 16 modes, so
+// that a warp streams 8 channels x 64 bytes of state with one coalesced
+// 16-byte access per thread; poles, residues and exp(log_pole) are loaded once
+// for all requests and every state load is issued before the gate phase.  The
+// readout keeps the halving tree of modal_readout16 exactly: modes s and s+8
+// meet across threads t and t+2, s and s+4 across t and t+1, the rest inside
+// thread 0.
+constexpr int IIR_R = 8;
+constexpr int IIR_CH = 64;
+constexpr int IIR_THREADS = 256;
+static_assert(IIR_R * IIR_CH / 4 <= IIR_THREADS, "one gate item per thread");
+
+__global__ void __launch_bounds__(IIR_THREADS, 3)
 decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
-  __shared__ float u_s[FAST_THREADS], x2_s[FAST_THREADS];
-  const int r = blockIdx.x;
-  const int hb0 = blockIdx.y * FAST_THREADS;
-  const int h = hb0 + threadIdx.x;
-  const long long cin = __ldg(A.conv_in_block + r);
-  const long long cout = __ldg(A.conv_out_block + r);
-  bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo;
-  if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
-    if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
-      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-    if (h < P.H) out[h] = __float2bfloat16_rn(0.0f);
-    return;
-  }
-  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
-  const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
-  const bool src_ok = block_ok(src, A.inner_state);
-  const bool dok = block_ok(dst, A.inner_state) && !(A.skip_null_writes && dst == A.null_block);
-  if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-  // state and parameters first: 16-byte loads in flight while the gate runs
-  float* st = static_cast<float*>(A.inner_state.data);
-  float s[16], pl[16], rs[16];
-  if (h < P.H) {
-    const float4* sp = reinterpret_cast<const float4*>(
-        st + (src_ok ? src : 0) * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride);
-    const float4* lp = reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h);
-    const float4* rr = reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 v = src_ok ? sp[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 a = __ldg(lp + q), b = __ldg(rr + q);
-      s[4 * q] = v.x; s[4 * q + 1] = v.y; s[4 * q + 2] = v.z; s[4 * q + 3] = v.w;
-      pl[4 * q] = a.x; pl[4 * q + 1] = a.y; pl[4 * q + 2] = a.z; pl[4 * q + 3] = a.w;
-      rs[4 * q] = b.x; rs[4 * q + 1] = b.y; rs[4 * q + 2] = b.z; rs[4 * q + 3] = b.w;
+  __shared__ long long route[4][IIR_R];  // cin, cout, src, dst per request
+  __shared__ float u_s[IIR_R][IIR_CH], x2_s[IIR_R][IIR_CH];
+  pdl_entry();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t = lane & 3;    // modes 4t .. 4t+3
+  const int cl = warp * 8 + (lane >> 2);  // channel within the block
+  const int hb = blockIdx.x * IIR_CH;
+  const int h = hb + cl;     // H % 64 == 0: always a valid channel
+  const int r0 = blockIdx.y * IIR_R;
+  const unsigned full = 0xffffffffu;
+  if (threadIdx.x < 4 * IIR_R) {
+    const int i = threadIdx.x % IIR_R, f = threadIdx.x / IIR_R, r = r0 + i;
+    long long v = -1;
+    if (r < A.num_reqs) {
+      if (f == 0) v = __ldg(A.conv_in_block + r);
+      else if (f == 1) v = __ldg(A.conv_out_block + r);
+      else if (f == 2) v = __ldg(A.in_slots + (long long)r * A.in_stride0);
+      else v = __ldg(A.out_slots + (long long)r * A.out_stride0);
     }
+    route[f][i] = v;
   }
-  // gate: 4 channels per thread on the first FAST_THREADS/4 threads
-  if (threadIdx.x < FAST_THREADS / 4 && hb0 + 4 * threadIdx.x < P.H) {
-    const bool write_conv = block_ok(cout, A.conv_state) &&
-                            !(A.skip_null_writes && cout == A.null_block);
-    float x2[4], u[4];
-    short_gate_q1<4>(P, A, r, hb0 + 4 * threadIdx.x, cin, cout, write_conv, x2, u);
+  float* st = static_cast<float*>(A.inner_state.data);
+  const float4 lp4 = __ldg(reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h) + t);
+  const float4 rs4 = __ldg(reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h) + t);
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  const float dval = Dg ? ldbf(Dg + h) : 0.0f;
+  __syncthreads();
+
+  // Request flags (uniform across the block) and every state load.
+  unsigned live = 0, zero = 0, dok = 0;
+  float4 sv[IIR_R];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      u_s[4 * threadIdx.x + c] = u[c];
-      x2_s[4 * threadIdx.x + c] = x2[c];
+  for (int i = 0; i < IIR_R; ++i) {
+    const long long cin = route[0][i], src = route[2][i], dst = route[3][i];
+    const bool lv = r0 + i < A.num_reqs;
+    const bool zr = lv && ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state));
+    const bool src_ok = block_ok(src, A.inner_state);
+    const bool dk = lv && !zr && block_ok(dst, A.inner_state) &&
+                    !(A.skip_null_writes && dst == A.null_block);
+    if (threadIdx.x == 0 && lv && (!block_ok(cin, A.conv_state) || (!zr && !src_ok)))
+      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+    live |= unsigned(lv) << i;
+    zero |= unsigned(zr) << i;
+    dok |= unsigned(dk) << i;
+    sv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lv && !zr && src_ok)
+      sv[i] = *reinterpret_cast<const float4*>(st + src * A.inner_state.block_stride +
+                                               (long long)h * A.inner_state.dim_stride + 4 * t);
+  }
+  // Gate phase: item = (request i, channels 4 c4 .. 4 c4 + 3 of the block).
+  if (threadIdx.x < IIR_R * IIR_CH / 4) {
+    const int i = threadIdx.x / (IIR_CH / 4), c4 = threadIdx.x % (IIR_CH / 4);
+    if ((live >> i) & 1u) {
+      float gx2[4] = {0.f, 0.f, 0.f, 0.f}, gu[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!((zero >> i) & 1u)) {
+        const long long cin = route[0][i], cout = route[1][i];
+        GateIn<4> gin;
+        gate_load<4>(P, A, r0 + i, hb + 4 * c4, cin, gin);
+        const bool write_conv =
+            block_ok(cout, A.conv_state) && !(A.skip_null_writes && cout == A.null_block);
+        gate_finish<4>(A, hb + 4 * c4, cout, write_conv, gin, gx2, gu);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        u_s[i][4 * c4 + e] = gu[e];
+        x2_s[i][4 * c4 + e] = gx2[e];
+      }
     }
   }
   __syncthreads();
-  if (h >= P.H) return;
-  const float u = u_s[threadIdx.x];
+  const float pole[4] = {expf(lp4.x), expf(lp4.y), expf(lp4.z), expf(lp4.w)};
+  const float res[4] = {rs4.x, rs4.y, rs4.z, rs4.w};
+  bf16* outp = static_cast<bf16*>(A.out);
 #pragma unroll
-  for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], expf(pl[q])), u);
-  if (dok) {
-    float4* dp = reinterpret_cast<float4*>(st + dst * A.inner_state.block_stride +
-                                           (long long)h * A.inner_state.dim_stride);
+  for (int i = 0; i < IIR_R; ++i) {
+    if (!((live >> i) & 1u)) continue;  // uniform
+    const long long orow = (long long)(r0 + i) * A.ldo;
+    if ((zero >> i) & 1u) {
+      if (t == 0) outp[orow + h] = __float2bfloat16_rn(0.0f);
+      continue;
+    }
+    const float u = u_s[i][cl], x2 = x2_s[i][cl];
+    float s4[4] = {sv[i].x, sv[i].y, sv[i].z, sv[i].w};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) dp[q] = make_float4(s[4 * q], s[4 * q + 1], s[4 * q + 2], s[4 * q + 3]);
+    for (int m = 0; m < 4; ++m) s4[m] = add_rn(mul_rn(s4[m], pole[m]), u);
+    if ((dok >> i) & 1u)
+      *reinterpret_cast<float4*>(st + route[3][i] * A.inner_state.block_stride +
+                                 (long long)h * A.inner_state.dim_stride + 4 * t) =
+          make_float4(s4[0], s4[1], s4[2], s4[3]);
+    float q[4], o[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) q[m] = mul_rn(s4[m], res[m]);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 2);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 8] (t < 2)
+#pragma unroll
+    for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 1);
+    if (t == 0) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 4]
+      q[0] = add_rn(q[0], q[2]);
+      q[1] = add_rn(q[1], q[3]);
+      float y = bf16r(add_rn(q[0], q[1]));
+      if (Dg) y = bf16r(y + bf16r(dval * u));
+      outp[orow + h] = __float2bfloat16_rn(bf16r(x2 * y));
+    }
   }
-  float y = bf16r(modal_readout16(s, rs));
-  const bf16* Dg = static_cast<const bf16*>(P.D);
-  if (Dg) y = bf16r(y + bf16r(ldbf(Dg + h) * u));
-  out[h] = __float2bfloat16_rn(bf16r(x2_s[threadIdx.x] * y));
 }
 
 static bool aligned_elems(const void* p, int64_t stride_elems, int elem_bytes, int vec_bytes) {
@@ -475,28 +557,28 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaS
     return fail(HYENA_ERR_UNSUPPORTED, "conv window wider than 8 columns");
   if (fast_path_ok(P, A)) {
     if (P.kind == HYENA_KIND_IIR && P.K == 16) {
-      dim3 g(A.num_reqs, (P.H + FAST_THREADS - 1) / FAST_THREADS);
-      decode_iir_q1_kernel<<<g, FAST_THREADS, 0, st>>>(P, A);
+      dim3 g(P.H / 64, (A.num_reqs + IIR_R - 1) / IIR_R);
+      launch_kernel(decode_iir_q1_kernel, dim3(g), dim3(IIR_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_iir_q1_kernel");
     }
     dim3 g(A.num_reqs, (P.H / 4 + FAST_THREADS - 1) / FAST_THREADS);
     if (P.kind == HYENA_KIND_FIR && P.K == 128) {
-      decode_fir_q1_kernel<128><<<g, FAST_THREADS, 0, st>>>(P, A);
+      launch_kernel(decode_fir_q1_kernel<128>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_fir_q1_kernel<128>");
     }
     if (P.kind == HYENA_KIND_FIR && P.K == 7) {
-      decode_fir_q1_kernel<7><<<g, FAST_THREADS, 0, st>>>(P, A);
+      launch_kernel(decode_fir_q1_kernel<7>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_fir_q1_kernel<7>");
     }
   }
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
   if (P.kind == HYENA_KIND_IIR) {
     if (P.K != 16) return fail(HYENA_ERR_UNSUPPORTED, "IIR decode supports modal order 16");
-    decode_kernel<HYENA_KIND_IIR, 16><<<grid, DEC_THREADS, 0, st>>>(P, A);
+    launch_kernel(decode_kernel<HYENA_KIND_IIR, 16>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
   } else if (P.K == 128) {
-    decode_kernel<HYENA_KIND_FIR, 128><<<grid, DEC_THREADS, 0, st>>>(P, A);
+    launch_kernel(decode_kernel<HYENA_KIND_FIR, 128>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
   } else if (P.K == 7) {
-    decode_kernel<HYENA_KIND_FIR, 7><<<grid, DEC_THREADS, 0, st>>>(P, A);
+    launch_kernel(decode_kernel<HYENA_KIND_FIR, 7>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
   } else {
     return fail(HYENA_ERR_UNSUPPORTED, "FIR decode supports K = 7 or 128");
   }

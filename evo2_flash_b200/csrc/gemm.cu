@@ -111,6 +111,13 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// Tile of a tensor map into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -209,6 +216,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
             const float* __restrict__ sa, const float* __restrict__ sb,
             const bf16* __restrict__ bias) {
+  pdl_trigger();
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = Cfg<BN>::TMEM_COLS;
@@ -249,6 +257,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   fence_after();
   const uint32_t tmem = S.tmem_base;
+  // While the previous kernel drains: this CTA's first weight tiles into L2
+  // (a prefetch cannot observe stale data: L2 is the point of coherence).
+  if (warp == 0 && lane == 0 && (int)blockIdx.x < total) {
+    const int n0 = ((int)blockIdx.x % n_tiles) * BN;
+    for (int kb = 0; kb < kblocks && kb < STAGES; ++kb) tma_prefetch_l2(&tmB, kb * KE, n0);
+  }
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -459,6 +474,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, bf16* __restrict__ out, int64_t ldo,
                     int M, int N, int K, const float* __restrict__ sa,
                     const float* __restrict__ sb, const bf16* __restrict__ bias) {
+  pdl_trigger();
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = pow2_cols<BN>();
@@ -512,6 +528,11 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
   __syncthreads();
   fence_after();
   const uint32_t tmem = S.tmem_base;
+  // While the previous kernel drains: this CTA's first weight tiles into L2.
+  if (warp == 0 && lane == 0) {
+    for (int kb = kb0; kb < kb1 && kb < kb0 + STAGES; ++kb) tma_prefetch_l2(&tmB, kb * KE, n0);
+  }
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -768,7 +789,7 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
   }
   const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
   dim3 grid((unsigned)(tiles < num_sms() ? tiles : num_sms()));
-  gemm_kernel<FP8, BN><<<grid, THREADS, smem, st>>>(ta, tb, static_cast<bf16*>(out), ldo, M, N,
+  launch_kernel(gemm_kernel<FP8, BN>, dim3(grid), dim3(THREADS), smem, st, 0u, ta, tb, static_cast<bf16*>(out), ldo, M, N,
                                                     K, sa, sb, static_cast<const bf16*>(bias));
   return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
 }
@@ -826,21 +847,9 @@ static int launch_cluster(const CUtensorMap& ta, const void* B, int64_t ldb, voi
   if (rc) return rc;
   if (!cluster_attr<FP8, BN>()) return check_launch("cudaFuncSetAttribute(gemm_cluster)");
   const int tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)splits, (unsigned)tiles, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = cluster_smem<FP8, BN>();
-  cfg.stream = st;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = (unsigned)splits;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, gemm_cluster_kernel<FP8, BN>, ta, tb, static_cast<bf16*>(out), ldo,
-                         M, N, K, sa, sb, static_cast<const bf16*>(bias)) != cudaSuccess)
-    return check_launch(FP8 ? "gemm_cluster_kernel<e4m3>" : "gemm_cluster_kernel<bf16>");
+  launch_kernel(gemm_cluster_kernel<FP8, BN>, dim3((unsigned)splits, (unsigned)tiles, 1),
+                dim3(THREADS), cluster_smem<FP8, BN>(), st, (unsigned)splits, ta, tb,
+                static_cast<bf16*>(out), ldo, M, N, K, sa, sb, static_cast<const bf16*>(bias));
   return check_launch(FP8 ? "gemm_cluster_kernel<e4m3>" : "gemm_cluster_kernel<bf16>");
 }
 

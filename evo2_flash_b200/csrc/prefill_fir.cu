@@ -143,6 +143,7 @@ __device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefi
 template <int K>
 __global__ void __launch_bounds__(FIR_THREADS, 2)
 fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
+  pdl_entry();
   constexpr int HIST = K - 1;
   static_assert(HIST + FIR_BT <= FIR_RING, "ring too small");
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -334,6 +335,7 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
 template <int K>
 __global__ void __launch_bounds__(128)
 prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
+  pdl_entry();
   const int j = blockIdx.x;
   const int h = blockIdx.y * 128 + threadIdx.x;
   if (h >= P.H) return;
@@ -433,11 +435,11 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   const long long want_ctas = 148LL * 8;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
   dim3 grid((A.T + rows - 1) / rows, groups);
-  fir_prefill_kernel<K><<<grid, FIR_THREADS, smem, st>>>(P, A, rows);
+  launch_kernel(fir_prefill_kernel<K>, dim3(grid), dim3(FIR_THREADS), smem, st, 0u, P, A, rows);
   int rc = check_launch("fir_prefill_kernel");
   if (rc) return rc;
   dim3 g2(A.num_segments, (P.H + 127) / 128);
-  prefill_state_kernel<K><<<g2, 128, 0, st>>>(P, A);
+  launch_kernel(prefill_state_kernel<K>, dim3(g2), dim3(128), 0, st, 0u, P, A);
   return check_launch("prefill_state_kernel");
 }
 
@@ -450,7 +452,7 @@ int fir_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
 int conv_state_update_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
                              cudaStream_t st) {
   dim3 g2(A.num_segments, (P.H + 127) / 128);
-  prefill_state_kernel<0><<<g2, 128, 0, st>>>(P, A);
+  launch_kernel(prefill_state_kernel<0>, dim3(g2), dim3(128), 0, st, 0u, P, A);
   return check_launch("prefill_state_kernel<0>");
 }
 

@@ -49,6 +49,7 @@ static HclWorkspace carve(void* ws, int nseg) {
 }
 
 __global__ void hcl_plan_kernel(const int32_t* qsl, int nseg, int32_t* chunk_base) {
+  pdl_entry();
   if (threadIdx.x != 0) return;
   int acc = 0;
   for (int j = 0; j < nseg; ++j) {
@@ -221,6 +222,7 @@ __device__ __forceinline__ float readout_pairs(const f2* s2, const f2* r2) {
 
 __global__ void __launch_bounds__(HCL_CG)
 hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
+  pdl_entry();
   __shared__ __align__(16) HclTile S;
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
@@ -246,6 +248,7 @@ hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, Hcl
 // the chunk's aggregate.
 __global__ void __launch_bounds__(128)
 hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
+  pdl_entry();
   const int j = blockIdx.x;
   const long long idx = (long long)blockIdx.y * 128 + threadIdx.x;  // h * 16 + s
   if (idx >= (long long)P.H * HCL_S) return;
@@ -277,6 +280,7 @@ hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWork
 
 __global__ void __launch_bounds__(HCL_CG)
 hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
+  pdl_entry();
   __shared__ __align__(16) HclTile S;
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
@@ -337,14 +341,14 @@ int hcl_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
   HclWorkspace W = carve(ws, A.num_segments);
   const int max_chunks = (A.T + HCL_C - 1) / HCL_C + A.num_segments;
   const int groups = P.H / HCL_CG;
-  hcl_plan_kernel<<<1, 32, 0, st>>>(A.query_start_loc, A.num_segments, W.chunk_base);
+  launch_kernel(hcl_plan_kernel, dim3(1), dim3(32), 0, st, 0u, A.query_start_loc, A.num_segments, W.chunk_base);
   int rc = check_launch("hcl_plan_kernel");
   if (rc) return rc;
-  hcl_aggregate_kernel<<<dim3(max_chunks, groups), HCL_CG, 0, st>>>(P, A, W);
+  launch_kernel(hcl_aggregate_kernel, dim3(max_chunks, groups), dim3(HCL_CG), 0, st, 0u, P, A, W);
   if ((rc = check_launch("hcl_aggregate_kernel"))) return rc;
-  hcl_carry_kernel<<<dim3(A.num_segments, (P.H * HCL_S + 127) / 128), 128, 0, st>>>(P, A, W);
+  launch_kernel(hcl_carry_kernel, dim3(A.num_segments, (P.H * HCL_S + 127) / 128), dim3(128), 0, st, 0u, P, A, W);
   if ((rc = check_launch("hcl_carry_kernel"))) return rc;
-  hcl_output_kernel<<<dim3(max_chunks, groups), HCL_CG, 0, st>>>(P, A, W);
+  launch_kernel(hcl_output_kernel, dim3(max_chunks, groups), dim3(HCL_CG), 0, st, 0u, P, A, W);
   if ((rc = check_launch("hcl_output_kernel"))) return rc;
   return conv_state_update_launch(P, A, st);
 }

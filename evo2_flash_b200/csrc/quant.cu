@@ -11,6 +11,7 @@ namespace hb {
 __global__ void __launch_bounds__(256)
 quant_e4m3_kernel(const bf16* __restrict__ x, int64_t ldx, uint8_t* __restrict__ q, int64_t ldq,
                   int M, int K, const float* __restrict__ scale) {
+  pdl_entry();
   const float sx = __ldg(scale);
   const int vpr = K / 8;
   const long long total = (long long)M * vpr;
@@ -40,7 +41,7 @@ int quant_e4m3_launch(const void* x, int64_t ldx, void* q, int64_t ldq, int M, i
   long long nb = (total + 255) / 256;
   if (nb > 148LL * 16) nb = 148LL * 16;
   const int blocks = (int)nb;
-  quant_e4m3_kernel<<<blocks, 256, 0, st>>>(static_cast<const bf16*>(x), ldx,
+  launch_kernel(quant_e4m3_kernel, dim3(blocks), dim3(256), 0, st, 0u, static_cast<const bf16*>(x), ldx,
                                             static_cast<uint8_t*>(q), ldq, M, K, scale);
   return check_launch("quant_e4m3_kernel");
 }

@@ -185,23 +185,56 @@ def test_verify_matches_oracle(kind, k):
         assert torch.equal(ds[1].cpu()[1:, : k - 1], ref_states[1][1:, : k - 1])
 
 
-def test_decode_null_block_row_is_zero_and_writes_nothing():
+@pytest.mark.parametrize("kind,k", [("hcm", 128), ("hcl", 16)])
+def test_decode_null_block_row_is_zero_and_writes_nothing(kind, k):
     from evo2_flash_b200 import ops
 
     H = 128
-    p = random_params("hcm", H, 128, seed=51)
-    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, "hcm")
+    p = random_params(kind, H, k, seed=51)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
     states = [s.to(DEV) for s in _random_states(H, 4, 2, seed=52)]
+    inner = 2 if kind == "hcl" else 1
     before = [s.clone() for s in states]
     z = torch.randn(2, 3 * H, device=DEV).to(torch.bfloat16)
     out = torch.full((2, H), 7.0, dtype=torch.bfloat16, device=DEV)
     idx = torch.tensor([0, 2], dtype=torch.int32, device=DEV)
-    ops.decode(w, z, out, idx, idx, idx[:, None], idx[:, None], states[0], states[1],
+    ops.decode(w, z, out, idx, idx, idx[:, None], idx[:, None], states[0], states[inner],
                zero_null_rows=True)
     torch.cuda.synchronize()
     assert torch.all(out[0] == 0)
-    assert torch.equal(states[0][0], before[0][0]) and torch.equal(states[1][0], before[1][0])
-    assert not torch.equal(states[1][2], before[1][2])
+    assert torch.equal(states[0][0], before[0][0]) and torch.equal(states[inner][0], before[inner][0])
+    assert not torch.equal(states[inner][2], before[inner][2])
+
+
+@pytest.mark.parametrize("kind,k", KINDS)
+def test_decode_many_requests_matches_oracle(kind, k):
+    """Enough requests and channels that every kernel covers several request /
+    channel groups, with the slots in scrambled order."""
+    from evo2_flash_b200 import ops
+
+    H, B = 512, 19
+    p = random_params(kind, H, k, seed=34)
+    po = params_to_oracle(p, kind, H, k)
+    states = _random_states(H, 41, 2, seed=35)
+    slots = torch.randperm(40, generator=torch.Generator().manual_seed(36))[:B].add(1).tolist()
+    g = torch.Generator().manual_seed(37)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
+    ds = [s.to(DEV) for s in states]
+    ref_states = [s.clone() for s in states]
+    for step in range(2):
+        z = (torch.randn(B, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+        ref = O.mixer_core(z, po, decode_meta(slots), ref_states, None, bf16_products=True)
+        out = torch.empty(B, H, dtype=torch.bfloat16, device=DEV)
+        idx = torch.tensor(slots, dtype=torch.int32, device=DEV)
+        ops.decode(w, z.to(DEV), out, idx, idx, idx[:, None], idx[:, None], ds[0],
+                   ds[2] if kind == "hcl" else ds[1], zero_null_rows=True)
+        torch.cuda.synchronize()
+        assert max_rel_err(out.cpu(), ref) < REL_TOL
+    assert torch.equal(ds[0].cpu(), ref_states[0])
+    if kind == "hcl":
+        assert max_rel_err(ds[2].cpu(), ref_states[2]) < 1e-5
+    else:
+        assert torch.equal(ds[1].cpu()[:, : k - 1], ref_states[1][:, : k - 1])
 
 
 def test_out_of_range_block_sets_flag_without_fault():
