@@ -13,6 +13,11 @@ Workloads (synthetic, seeded; no checkpoint or dataset is used):
 Multi-GPU (torchrun, one rank per GPU): every rank runs the same per-rank
 workload on its own sequences (independent replicas, weak scaling); only the
 timing reduction crosses ranks.
+  --workload tp40b  config 5: the 40B-shape triple (H=8192, fp8 in_proj
+           8192->24576) channel-sharded over the ranks (tensor parallel, strong
+           scaling), one 262144-token sequence prefilled in chunks whose
+           all-reduces overlap the next chunks' kernels, then batch-1 decode
+           steps.  `value` = prefill tokens/s of the whole job.
 
 `--impl reference` times the reference algorithm's CPU implementation (the
 oracle port in oracle/, all host threads) on a bounded sample of the same
@@ -387,6 +392,125 @@ def cpu_baseline_sample(tokens_per_step, steps, warmup):
     return tokens_per_step / med, threads, med
 
 
+
+# ---------------------------------------------------------------- config 5 (TP)
+H40 = 8192
+TP_TOKENS = 262144
+
+
+def run_tp40b(args, world, rank, device, dist_ok):
+    """40B-shape triple, channel-sharded over `world` ranks; chunked prefill with
+    the row-parallel all-reduces in flight under the following chunks, then
+    batch-1 decode steps (eager, one all-reduce per layer)."""
+    import torch.distributed as dist
+
+    from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer, set_forward_metadata
+    from evo2_flash_b200.synthetic import mixer_tensors
+
+    group = dist.group.WORLD if dist_ok else None
+    cfg = SimpleNamespace(hidden_size=H40, short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=True)
+    # identical (seeded, on-device) full tensors on every rank; each keeps its shard
+    gen = torch.Generator(device=device).manual_seed(5)
+    table = torch.randn(512, H40, generator=gen, device=device)
+    lut = torch.tensor([65, 67, 71, 84], device=device)
+    toks = lut[torch.randint(0, 4, (TP_TOKENS,), generator=gen, device=device)]
+    x = rmsnorm(table[toks])
+    sx = (x[:4096].float().abs().amax() / 448.0).reshape(1)
+    layers = []
+    for i, (kind, k) in enumerate(TRIPLE):
+        t = mixer_tensors(kind, H40, k, 200 + i, fp8=True, device=device)
+        t["in_proj.input_scale"] = sx
+        kw = dict(tp_rank=rank, tp_size=world, tp_group=group, device=device)
+        m = (HyenaIIRMixer(cfg, i, prefix=f"tp.{i}", **kw) if kind == "hcl"
+             else HyenaFIRMixer(cfg, i, prefix=f"tp.{i}", k_inner=k, **kw))
+        m.load_full_weights(t)
+        del t
+        m.allocate_state(2, device)
+        layers.append(m)
+    chunk = args.tp_chunk
+    nchunks = TP_TOKENS // chunk
+    metas = [prefill_meta([chunk], [1], device, init=[c > 0]) for c in range(nchunks)]
+
+    def prefill_step():
+        pend = []
+        for c in range(nchunks):
+            xc = x[c * chunk:(c + 1) * chunk]
+            with set_forward_metadata(metas[c]):
+                for m in layers:
+                    pend.append(m.forward_async(xc))
+        for p in pend:
+            p.wait()
+
+    for _ in range(args.warmup):
+        prefill_step()
+    torch.cuda.synchronize()
+    if dist_ok:
+        dist.barrier()
+    with Clocks(torch.cuda.current_device()) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            prefill_step()
+        e1.record()
+        torch.cuda.synchronize()
+    t_step = e0.elapsed_time(e1) / args.steps
+    if dist_ok:
+        tt = torch.tensor([t_step], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_step = float(tt.item())
+
+    # batch-1 decode after the prefill (state continues from the last chunk)
+    dmeta = decode_meta([1], device)
+    xd = rmsnorm(table[lut[torch.randint(0, 4, (args.tp_decode_steps + args.warmup,),
+                                         generator=gen, device=device)]])
+
+    def decode_step(i):
+        with set_forward_metadata(dmeta):
+            for m in layers:
+                m(xd[i:i + 1])
+
+    for i in range(args.warmup):
+        decode_step(i)
+    torch.cuda.synchronize()
+    if dist_ok:
+        dist.barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for i in range(args.tp_decode_steps):
+        decode_step(args.warmup + i)
+    d1.record()
+    torch.cuda.synchronize()
+    d_ms = d0.elapsed_time(d1) / args.tp_decode_steps
+    if dist_ok:
+        tt = torch.tensor([d_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        d_ms = float(tt.item())
+
+    f_gemm = 3 * (2 * TP_TOKENS * H40 * 3 * H40 + 2 * TP_TOKENS * H40 * H40)  # whole job
+    value = TP_TOKENS / (t_step * 1e-3)
+    line = {
+        "metric": METRIC + " (config 5: 40B-shape triple, tensor parallel)",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "e4m3/bf16",
+        "data": "synthetic (seeded ACGT, random-init weights)",
+        "config": {"workload": "config5: HCS+HCM+HCL mixer triple, 40B shape (H=8192), "
+                               "channel-sharded (column-parallel in_proj, row-parallel out_proj "
+                               "+ one all-reduce per layer)",
+                   "hidden": H40, "global_batch": 1, "seq_len": TP_TOKENS,
+                   "parallelism": f"tp{world}", "prefill_chunk": chunk,
+                   "l2": "inputs larger than L2 (x 4.3 GB)"},
+        "tok_per_s_per_gpu": value / world,
+        "projection_tflops_per_gpu": f_gemm / world / (t_step * 1e-3) / 1e12,
+        "decode": {"batch": 1, "ms_per_step": d_ms, "tok_per_s": 1e3 / d_ms,
+                   "steps": args.tp_decode_steps, "graph": False},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -401,6 +525,9 @@ def main():
     ap.add_argument("--only", choices=["prefill", "decode"], default=None,
                     help="run one workload (small profiling cases)")
     ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per rank")
+    ap.add_argument("--workload", choices=["triple", "tp40b"], default="triple")
+    ap.add_argument("--tp-chunk", type=int, default=32768, help="tp40b prefill chunk (tokens)")
+    ap.add_argument("--tp-decode-steps", type=int, default=256)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -436,6 +563,13 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    if args.workload == "tp40b":
+        run_tp40b(args, world, rank, device, dist_ok)
+        if dist_ok:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     from evo2_flash_b200 import ops as ops_mod
 

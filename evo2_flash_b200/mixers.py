@@ -33,7 +33,7 @@ from torch import nn
 
 from . import ops
 from .forward_context import lookup
-from .parallel import all_reduce_partial, shard_mixer_tensors
+from .parallel import PendingReduce, all_reduce_partial, all_reduce_partial_async, shard_mixer_tensors
 
 HYENA_MIXER_OP = "evo2_b200::hyena_mixer"
 
@@ -329,27 +329,41 @@ class HyenaMixerBase(nn.Module):
                         m.state_indices_tensor_p[: int(m.num_prefills)], conv, inner)
         return g
 
-    def _out_proj(self, g):
+    def _out_proj(self, g, async_reduce=False, finish=None):
         out, _ = self.out_proj(g)
         if self.tp_size > 1:
+            if async_reduce:
+                return all_reduce_partial_async(out, self.out_proj.bias, self.tp_group, finish)
             out = all_reduce_partial(out, self.out_proj.bias, self.tp_group)
+        if async_reduce:
+            return PendingReduce(out, None, None, finish)
         return out
 
-    def _forward_impl(self, hidden_states, token_ids=None):
+    def _forward_impl(self, hidden_states, token_ids=None, async_reduce=False):
         m = self._meta()
         if m is None:
-            return self._profile_run(hidden_states, token_ids)
+            out = self._profile_run(hidden_states, token_ids)
+            return PendingReduce(out, None, None) if async_reduce else out
         self._repair_resumed_prefill_state(m)
         accepted = self._resolve_accepted(m)  # before any state is written
         nd, npt = int(m.num_decode_tokens), int(m.num_prefill_tokens)
         z = self._project(hidden_states[: nd + npt], token_ids)
         g = self._run_core(z, m, accepted)
         self._record_stamps(m)
-        out = self._out_proj(g)
-        return self._unpad(out, hidden_states, nd + npt)
+        finish = lambda out: self._unpad(out, hidden_states, nd + npt)  # noqa: E731
+        if async_reduce:
+            return self._out_proj(g, True, finish)
+        return finish(self._out_proj(g))
 
     def forward(self, hidden_states, token_ids=None):
         return self._forward_impl(hidden_states, token_ids)
+
+    def forward_async(self, hidden_states, token_ids=None) -> PendingReduce:
+        """forward() with the channel-sharded all-reduce left in flight: returns a
+        PendingReduce whose wait() yields the output.  Lets a caller overlap one
+        step's (or chunk's) all-reduce with the next one's kernels; with
+        tp_size == 1 the result is complete already."""
+        return self._forward_impl(hidden_states, token_ids, async_reduce=True)
 
     @staticmethod
     def _unpad(out, hidden_states, n_actual):

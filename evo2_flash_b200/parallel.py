@@ -60,3 +60,29 @@ def all_reduce_partial(out: torch.Tensor, bias: torch.Tensor | None, group=None)
     """Completes a row-parallel out_proj: sum the ranks' partials, add the bias once."""
     dist.all_reduce(out, group=group)
     return out if bias is None else out + bias
+
+
+class PendingReduce:
+    """A row-parallel out_proj whose all-reduce is in flight (NCCL runs on its
+    own stream).  `wait()` orders the caller's current stream after the reduce,
+    adds the bias once and returns the completed output; until then the caller
+    may launch other work (the next chunk or layer), which the reduce overlaps."""
+
+    def __init__(self, out, bias, work, finish=None):
+        self._out, self._bias, self._work, self._finish = out, bias, work, finish
+        self._done = None
+
+    def wait(self) -> torch.Tensor:
+        if self._done is None:
+            if self._work is not None:
+                self._work.wait()
+            out = self._out if self._bias is None else self._out + self._bias
+            self._done = self._finish(out) if self._finish is not None else out
+        return self._done
+
+
+def all_reduce_partial_async(out: torch.Tensor, bias: torch.Tensor | None, group=None,
+                             finish=None) -> PendingReduce:
+    """all_reduce_partial with the collective left in flight (see PendingReduce)."""
+    work = dist.all_reduce(out, group=group, async_op=True)
+    return PendingReduce(out, bias, work, finish)

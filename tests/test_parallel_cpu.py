@@ -109,3 +109,41 @@ def test_channel_sharded_mixer_equals_unsharded(kind, k, tmp_path):
         a, b = got[f"rows_{r}"]
         assert torch.equal(got[f"s1_{r}"], states[1][:, :, a:b])
         assert max_rel_err(got[f"s2_{r}"], states[2][:, a:b]) < 1e-6
+
+
+def _async_worker(rank, world, port, out_dir):
+    from evo2_flash_b200.parallel import all_reduce_partial_async
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(100 + rank)
+        parts = [torch.randn(6, 8, generator=g) for _ in range(3)]
+        bias = torch.arange(8, dtype=torch.float32)
+        pend = [all_reduce_partial_async(p.clone(), bias, finish=lambda t: t[:5]) for p in parts]
+        outs = [pr.wait() for pr in pend]
+        assert all(pr.wait() is o for pr, o in zip(pend, outs))  # wait() is idempotent
+        torch.save({"parts": parts, "outs": outs}, os.path.join(out_dir, f"a{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_async_all_reduce_completes_partials_once(tmp_path):
+    """Several row-parallel reduces in flight at once; each wait() returns the
+    sum over ranks plus the bias once, through the caller's finishing step."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_async_worker, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+        assert pr.exitcode == 0
+    res = [torch.load(tmp_path / f"a{r}.pt") for r in range(world)]
+    bias = torch.arange(8, dtype=torch.float32)
+    for i in range(3):
+        want = (res[0]["parts"][i] + res[1]["parts"][i] + bias)[:5]
+        for r in range(world):
+            assert torch.allclose(res[r]["outs"][i], want)
