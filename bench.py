@@ -18,6 +18,10 @@ timing reduction crosses ranks.
            scaling), one 262144-token sequence prefilled in chunks whose
            all-reduces overlap the next chunks' kernels, then batch-1 decode
            steps.  `value` = prefill tokens/s of the whole job.
+  --workload cp40b  config 5 with context parallelism instead: every rank runs
+           the full-width triple on its contiguous slice of the 262144-token
+           sequence (FIR layers with a K+1-row halo, the LI layer in two passes
+           around one all-gather of (H, 16) slice states); strong scaling.
 
 `--impl reference` times the reference algorithm's CPU implementation (the
 oracle port in oracle/, all host threads) on a bounded sample of the same
@@ -407,7 +411,15 @@ def run_tp40b(args, world, rank, device, dist_ok):
     from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer, set_forward_metadata
     from evo2_flash_b200.synthetic import mixer_tensors
 
+    from evo2_flash_b200 import ops
+
     group = dist.group.WORLD if dist_ok else None
+    reserve = args.tp_reserve_sms if world > 1 else 0
+    if world > 1 and not args.tp_chaining:
+        ops.set_launch_chaining(False)
+    if reserve:
+        props = torch.cuda.get_device_properties(device)
+        ops.set_gemm_max_ctas(props.multi_processor_count - reserve)
     cfg = SimpleNamespace(hidden_size=H40, short_filter_length=3, hcm_filter_length=128,
                           state_size=16, use_fp8_input_projections=True)
     # identical (seeded, on-device) full tensors on every rank; each keeps its shard
@@ -500,11 +512,94 @@ def run_tp40b(args, world, rank, device, dist_ok):
                                "+ one all-reduce per layer)",
                    "hidden": H40, "global_batch": 1, "seq_len": TP_TOKENS,
                    "parallelism": f"tp{world}", "prefill_chunk": chunk,
+                   "gemm_sms_left_to_collectives": reserve,
+                   "launch_chaining": bool(args.tp_chaining) or world == 1,
                    "l2": "inputs larger than L2 (x 4.3 GB)"},
         "tok_per_s_per_gpu": value / world,
         "projection_tflops_per_gpu": f_gemm / world / (t_step * 1e-3) / 1e12,
         "decode": {"batch": 1, "ms_per_step": d_ms, "tok_per_s": 1e3 / d_ms,
                    "steps": args.tp_decode_steps, "graph": False},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+
+
+
+def run_cp40b(args, world, rank, device, dist_ok):
+    """40B-shape triple, one 262144-token sequence split into `world`
+    contiguous slices (context parallel); per layer the only collective is the
+    LI layer's all-gather of (H, 16) slice states."""
+    from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer
+    from evo2_flash_b200.context_parallel import cp_prefill, dist_gather, halo_rows
+    from evo2_flash_b200.synthetic import mixer_tensors
+
+    cfg = SimpleNamespace(hidden_size=H40, short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=True)
+    gen = torch.Generator(device=device).manual_seed(5)
+    table = torch.randn(512, H40, generator=gen, device=device)
+    lut = torch.tensor([65, 67, 71, 84], device=device)
+    toks = lut[torch.randint(0, 4, (TP_TOKENS,), generator=gen, device=device)]
+    L = TP_TOKENS // world
+    lo = rank * L
+    halo = 136  # >= every layer's halo_rows (129 for K = 128)
+    x_src = table[toks[max(0, lo - halo):lo + L]]
+    x_all = rmsnorm(x_src)
+    x_local = x_all[x_all.shape[0] - L:]
+    x_halo = None if rank == 0 else x_all[:x_all.shape[0] - L]
+    calib = rmsnorm(table[toks[:4096]])
+    sx = (calib.float().abs().amax() / 448.0).reshape(1)
+    layers = []
+    for i, (kind, k) in enumerate(TRIPLE):
+        t = mixer_tensors(kind, H40, k, 200 + i, fp8=True, device=device)
+        t["in_proj.input_scale"] = sx
+        m = (HyenaIIRMixer(cfg, i, prefix=f"cp.{i}", device=device) if kind == "hcl"
+             else HyenaFIRMixer(cfg, i, prefix=f"cp.{i}", k_inner=k, device=device))
+        m.load_full_weights(t)
+        del t
+        m.allocate_state(2, device)
+        assert halo >= halo_rows(m)
+        layers.append(m)
+    if dist_ok:
+        gather = dist_gather()
+    else:
+        gather = lambda t: t[None]  # noqa: E731
+
+    def step():
+        for m in layers:
+            cp_prefill(m, x_local, x_halo, rank, gather)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist_ok:
+        torch.distributed.barrier()
+    with Clocks(torch.cuda.current_device()) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    t_step = e0.elapsed_time(e1) / args.steps
+    if dist_ok:
+        tt = torch.tensor([t_step], device=device)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_step = float(tt.item())
+    value = TP_TOKENS / (t_step * 1e-3)
+    line = {
+        "metric": METRIC + " (config 5: 40B-shape triple, context parallel)",
+        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "e4m3/bf16",
+        "data": "synthetic (seeded ACGT, random-init weights)",
+        "config": {"workload": "config5: HCS+HCM+HCL mixer triple, 40B shape (H=8192), one "
+                               "sequence split into contiguous per-rank slices (FIR halo rows, "
+                               "LI slice states all-gathered)",
+                   "hidden": H40, "global_batch": 1, "seq_len": TP_TOKENS,
+                   "parallelism": f"cp{world}", "slice_tokens": L, "halo_rows": halo,
+                   "l2": "inputs larger than L2"},
+        "tok_per_s_per_gpu": value / world,
         "clocks": clk.summary(),
     }
     if rank == 0:
@@ -525,9 +620,13 @@ def main():
     ap.add_argument("--only", choices=["prefill", "decode"], default=None,
                     help="run one workload (small profiling cases)")
     ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per rank")
-    ap.add_argument("--workload", choices=["triple", "tp40b"], default="triple")
+    ap.add_argument("--workload", choices=["triple", "tp40b", "cp40b"], default="triple")
     ap.add_argument("--tp-chunk", type=int, default=32768, help="tp40b prefill chunk (tokens)")
     ap.add_argument("--tp-decode-steps", type=int, default=256)
+    ap.add_argument("--tp-reserve-sms", type=int, default=0,
+                    help="tp40b with N > 1: SMs the projection GEMMs leave to the all-reduces")
+    ap.add_argument("--tp-chaining", type=int, default=1,
+                    help="tp40b with N > 1: programmatic dependent launch between kernels (1/0)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -562,10 +661,15 @@ def main():
     if dist_ok:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        kw = {}
+        if args.workload == "tp40b":  # collectives overlap compute: schedule their CTAs first
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+            kw["pg_options"] = opts
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device, **kw)
 
-    if args.workload == "tp40b":
-        run_tp40b(args, world, rank, device, dist_ok)
+    if args.workload in ("tp40b", "cp40b"):
+        (run_tp40b if args.workload == "tp40b" else run_cp40b)(args, world, rank, device, dist_ok)
         if dist_ok:
             dist.barrier()
             dist.destroy_process_group()

@@ -110,6 +110,8 @@ SIGNATURES = {
                                   C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_size_t, C.c_void_p]),
     "hyena_gemm_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "hyena_set_gemm_max_ctas": (None, [C.c_int32]),
+    "hyena_set_launch_chaining": (None, [C.c_int32]),
 }
 
 _lock = threading.Lock()

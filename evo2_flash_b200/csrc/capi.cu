@@ -1,4 +1,5 @@
 // C ABI entry points: argument validation, dispatch, thread-local error text.
+#include <atomic>
 #include <cstdio>
 
 #include "common.cuh"
@@ -6,6 +7,9 @@
 namespace hb {
 
 static thread_local std::string g_last_error;
+static std::atomic<bool> g_launch_chaining{true};
+
+bool launch_chaining() { return g_launch_chaining.load(std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -34,6 +38,7 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
                      int64_t ldo, int M, int N, int K, const void* bias, void* ws,
                      size_t ws_bytes, cudaStream_t st);
 size_t gemm_workspace_size(int M, int N, int K, bool fp8);
+void gemm_set_max_ctas(int n);
 
 static int check_params(const hyena_layer_params* p) {
   HB_REQUIRE(p != nullptr, "null layer params");
@@ -66,6 +71,12 @@ using namespace hb;
 extern "C" {
 
 int hyena_abi_version(void) { return HYENA_ABI_VERSION; }
+
+void hyena_set_gemm_max_ctas(int32_t n) { hb::gemm_set_max_ctas(n); }
+
+void hyena_set_launch_chaining(int32_t enable) {
+  hb::g_launch_chaining.store(enable != 0, std::memory_order_relaxed);
+}
 
 const char* hyena_last_error(void) { return g_last_error.c_str(); }
 

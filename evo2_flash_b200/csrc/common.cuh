@@ -43,6 +43,10 @@ __device__ __forceinline__ void pdl_entry() {
   pdl_wait();
 }
 
+// Process-wide switch for the programmatic-serialisation attribute (on by
+// default; hyena_set_launch_chaining).
+bool launch_chaining();
+
 // cudaLaunchKernelEx with the programmatic-serialisation attribute (and a
 // 1-D cluster of `cluster_x` CTAs when cluster_x > 0).
 template <typename... KArgs, typename... Args>
@@ -55,9 +59,11 @@ inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, 
   cfg.stream = st;
   cudaLaunchAttribute at[2];
   unsigned n = 0;
-  at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[n].val.programmaticStreamSerializationAllowed = 1;
-  ++n;
+  if (launch_chaining()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   if (cluster_x > 0) {
     at[n].id = cudaLaunchAttributeClusterDimension;
     at[n].val.clusterDim.x = cluster_x;

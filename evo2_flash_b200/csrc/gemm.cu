@@ -26,6 +26,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace hb {
@@ -761,6 +763,11 @@ static int make_map(CUtensorMap* m, const void* base, bool fp8, uint64_t inner, 
   return HYENA_OK;
 }
 
+// Upper bound on the CTAs of a persistent GEMM (0 = one per SM): leaves SMs
+// free for kernels that must run alongside, such as collectives on another
+// stream.  Set through hyena_set_gemm_max_ctas.
+static std::atomic<int> g_max_ctas{0};
+
 static int num_sms() {
   static int sms = 0;
   if (sms == 0) {
@@ -788,7 +795,10 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
     attr = true;
   }
   const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
-  dim3 grid((unsigned)(tiles < num_sms() ? tiles : num_sms()));
+  long long cap = num_sms();
+  const int lim = g_max_ctas.load(std::memory_order_relaxed);
+  if (lim > 0 && lim < cap) cap = lim;
+  dim3 grid((unsigned)(tiles < cap ? tiles : cap));
   launch_kernel(gemm_kernel<FP8, BN>, dim3(grid), dim3(THREADS), smem, st, 0u, ta, tb, static_cast<bf16*>(out), ldo, M, N,
                                                     K, sa, sb, static_cast<const bf16*>(bias));
   return check_launch(FP8 ? "gemm_kernel<e4m3>" : "gemm_kernel<bf16>");
@@ -955,6 +965,8 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
   (void)ws_bytes;
   return gemm::launch<false>(A, lda, B, ldb, out, ldo, M, N, K, nullptr, nullptr, bias, st);
 }
+
+void gemm_set_max_ctas(int n) { gemm::g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
 
 size_t gemm_workspace_size(int M, int N, int K, bool fp8) {
   (void)M;

@@ -264,6 +264,18 @@ def gemm_e4m3(a, b, scale_a, scale_b, out=None):
     return out
 
 
+def set_gemm_max_ctas(n: int) -> None:
+    """Caps the CTAs of the large-M GEMMs (0: one per SM) so that collectives
+    running on another stream find free SMs (hyena_set_gemm_max_ctas)."""
+    _lib.load().hyena_set_gemm_max_ctas(int(n))
+
+
+def set_launch_chaining(enable: bool) -> None:
+    """Programmatic dependent launch between this library's kernels on/off
+    (hyena_set_launch_chaining; on by default)."""
+    _lib.load().hyena_set_launch_chaining(int(bool(enable)))
+
+
 def _gemm_workspace(lib, M, N, K, fp8, device):
     """Workspace the library asks for at this shape (none at present: small-M
     GEMMs reduce their K slices inside a thread-block cluster)."""

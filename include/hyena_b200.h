@@ -195,6 +195,21 @@ HYENA_API int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t
  * callers written against ABI version 2 keep working).  fp8 != 0 selects e4m3. */
 HYENA_API size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8);
 
+/* Caps the CTAs of the persistent (large-M) GEMMs at n (n <= 0: one per SM,
+ * the default).  Process-wide.  A caller that overlaps GEMMs with collectives
+ * on another stream (channel-sharded out_proj all-reduces) leaves SMs free for
+ * them this way.  No counterpart in the reference, which has no tensor
+ * parallelism (mixers.py:38-41). */
+HYENA_API void hyena_set_gemm_max_ctas(int32_t n);
+
+/* enable != 0 (the default): kernels are launched with programmatic dependent
+ * launch, so each can be scheduled while its stream predecessor drains (every
+ * kernel still waits for that predecessor before touching global memory).
+ * enable == 0: plain stream order, for callers that overlap these kernels with
+ * work on other streams and want SMs released between kernels.  Process-wide.
+ * No counterpart in the reference. */
+HYENA_API void hyena_set_launch_chaining(int32_t enable);
+
 /* ---------------------------------------------------------------- misc */
 HYENA_API int hyena_abi_version(void);
 HYENA_API const char* hyena_last_error(void);
