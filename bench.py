@@ -85,19 +85,25 @@ def layer_params(kind, k, seed, device):
 TRIPLE = (("hcs", 7), ("hcm", 128), ("hcl", 16))
 
 
-def build_triple(device, input_scale, num_blocks):
+def build_triple(device, input_scale, num_blocks, num_spec=0, params=None):
+    """The config-2/3 triple (params: reuse the (m, p) list of another triple's
+    weights; num_spec > 0: speculative layout with 1 + num_spec verifier slots)."""
     from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer
 
     cfg = SimpleNamespace(hidden_size=H, short_filter_length=3, hcm_filter_length=128,
                           state_size=16, use_fp8_input_projections=True)
     layers = []
     for i, (kind, k) in enumerate(TRIPLE):
-        p = layer_params(kind, k, 100 + i, "cpu")
-        p["in_proj.input_scale"] = input_scale.reshape(1)
-        if kind == "hcl":
-            m = HyenaIIRMixer(cfg, i, prefix=f"triple.{i}", device=device)
+        if params is None:
+            p = layer_params(kind, k, 100 + i, "cpu")
+            p["in_proj.input_scale"] = input_scale.reshape(1)
         else:
-            m = HyenaFIRMixer(cfg, i, prefix=f"triple.{i}", k_inner=k, device=device)
+            p = params[i][1]
+        kw = dict(num_spec=num_spec, device=device)
+        if kind == "hcl":
+            m = HyenaIIRMixer(cfg, i, prefix=f"triple.{i}", **kw)
+        else:
+            m = HyenaFIRMixer(cfg, i, prefix=f"triple.{i}", k_inner=k, **kw)
         m.load_full_weights({kk: v.to(device) for kk, v in p.items()})
         m.allocate_state(num_blocks, device)
         layers.append((m, p))
@@ -348,6 +354,85 @@ def run_decode(layers, table, device, steps, warmup, gen):
     ms = e0.elapsed_time(e1)
     del graph
     return ms / steps, lengths
+
+
+def run_verify(layers, table, device, steps, warmup, gen, q=4):
+    """Config 3's speculative verify: the same 128 ragged prompts prefilled into
+    a speculative-layout triple (1 + 3 verifier slots per request), then steps
+    of q = 4 positions per request (anchor + 3 drafts of random ACGT) whose
+    accepted counts are drawn uniformly from 1..4 and resolved from the state's
+    position stamps, replayed from one CUDA graph."""
+    from evo2_flash_b200 import set_forward_metadata
+
+    spec = build_triple(device, None, 1 + DECODE_B * q, num_spec=q - 1, params=layers)
+    lengths = torch.randint(256, 4097, (DECODE_B,), generator=gen).tolist()
+    slots = torch.arange(1, 1 + DECODE_B * q, dtype=torch.int32).view(DECODE_B, q)
+    x = embed_norm(acgt_tokens(sum(lengths), gen), table, device)
+    with set_forward_metadata(prefill_meta(lengths, slots[:, 0].tolist(), device)):
+        for m, _ in spec:
+            m(x)
+    del x
+    nsteps = warmup + steps
+    xs = embed_norm(acgt_tokens(DECODE_B * q * nsteps, gen), table, device).view(nsteps, DECODE_B * q, H)
+    acc = torch.randint(1, q + 1, (nsteps, DECODE_B), generator=gen).to(device)
+    computed = torch.tensor(lengths, dtype=torch.int32, device=device)
+    meta = SimpleNamespace(
+        num_decodes=DECODE_B, num_decode_tokens=DECODE_B * q, num_prefills=0,
+        num_prefill_tokens=0,
+        query_start_loc_p=torch.zeros(1, dtype=torch.int32, device=device),
+        has_initial_states_p=torch.zeros(0, dtype=torch.bool, device=device),
+        state_indices_tensor_p=torch.zeros(0, dtype=torch.int32, device=device),
+        state_indices_tensor_d=slots.to(device),
+        query_start_loc_d=torch.arange(0, DECODE_B * q + 1, q, dtype=torch.int32, device=device),
+        num_accepted_tokens=None, num_computed_tokens_d=computed,
+        seq_lens=torch.zeros(DECODE_B, dtype=torch.int32, device=device))
+    x_static = torch.empty(DECODE_B * q, H, dtype=torch.bfloat16, device=device)
+
+    def step():
+        with set_forward_metadata(meta):
+            for m, _ in spec:
+                m(x_static)
+
+    def advance(i):  # the previous step accepted acc[i] tokens per request
+        x_static.copy_(xs[i])
+        computed.add_(acc[i].to(torch.int32))
+
+    x_static.copy_(xs[0])  # first step: accepted = 1 (stamp = prompt length)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for i in range(warmup):
+        advance(i)
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, nsteps):
+        advance(i)
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del graph, spec
+    return ms
+
+
+def verify_bytes_per_step(q=4):
+    """Algorithmic HBM bytes of one verify step of the triple at B=128: weights
+    once, per request and layer the accepted snapshot read and q snapshots
+    written (S1 6 / 127 columns for HCS / HCM, S2 16 modes for HCL), the S0
+    window (2 + q - 1 columns) read and written, activations in and out."""
+    w_in = 3 * (3 * H * H)
+    w_out = 3 * (H * H * 2 + H * 2)
+    per_req = 3 * (2 * (2 + q - 1) * 3 * H * 2)
+    per_req += (1 + q) * (6 * H * 4 + 127 * H * 4 + 17 * H * 4)
+    act = 3 * DECODE_B * q * (H * 2 + 3 * H * 2 * 2 + H * 2 * 2 + H * 2)
+    return w_in + w_out + DECODE_B * per_req + act
 
 
 def decode_bytes_per_step():
@@ -745,6 +830,18 @@ def main():
                   "hbm_frac": dbytes / (d_ms * 1e-3) / 1e9 / hbm,
                   "bytes_per_step": dbytes,
                   "prompt_tokens": int(sum(lengths))}
+        v_ms = run_verify(layers, table, device, max(10, args.decode_steps // 4), args.warmup,
+                          torch.Generator().manual_seed(4 + rank))
+        if dist_ok:
+            tt = torch.tensor([v_ms], device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            v_ms = float(tt.item())
+        vbytes = verify_bytes_per_step()
+        decode["verify"] = {"q": 4, "ms_per_step": v_ms, "positions_per_s": world * DECODE_B * 4 / (v_ms * 1e-3),
+                            "accepted": "uniform 1..4, resolved from position stamps",
+                            "hbm_gbs": vbytes / (v_ms * 1e-3) / 1e9,
+                            "hbm_frac": vbytes / (v_ms * 1e-3) / 1e9 / hbm,
+                            "bytes_per_step": vbytes, "graph": True}
 
     e2e = None
     if not args.no_e2e:

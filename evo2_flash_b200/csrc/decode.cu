@@ -552,6 +552,228 @@ static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A
          aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % 4 == 0;
 }
 
+// FIR verify (q <= VQ positions per request, speculative windows): one thread
+// per (request, 4 channels).  The short filter runs per column exactly as in
+// decode_kernel; the inner FIR streams the accepted snapshot once with 16-byte
+// loads (4 channels), keeps the last VQ taps' weights in registers, and writes
+// every verifier snapshot with 16-byte stores.  Same arithmetic and order as
+// decode_kernel (fp32 FMA over taps oldest first, then the verified tokens).
+constexpr int VQ = 4;
+
+template <int K>
+__global__ void __launch_bounds__(FAST_THREADS)
+decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  pdl_entry();
+  constexpr int HIST = K - 1;
+  constexpr int U = 8;  // window columns in flight
+  const int r = blockIdx.x;
+  const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
+  if (h >= P.H) return;
+  int t0, n;
+  if (A.token_start) {
+    t0 = __ldg(A.token_start + r);
+    n = __ldg(A.token_start + r + 1) - t0;
+  } else {
+    t0 = r;
+    n = 1;
+  }
+  if (n <= 0) return;
+  if (n > A.q || n > VQ) {
+    if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+    n = min(A.q, VQ);
+  }
+  const int accepted = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+  const int off = accepted - 1;
+  const long long cin = __ldg(A.conv_in_block + r);
+  const long long cout = __ldg(A.conv_out_block + r);
+  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
+  long long dst[VQ];
+  bool dok[VQ];
+#pragma unroll
+  for (int p = 0; p < VQ; ++p) {
+    dst[p] = p < n ? __ldg(A.out_slots + (long long)r * A.out_stride0 + (long long)p * A.out_stride1) : 0;
+    dok[p] = p < n && block_ok(dst[p], A.inner_state) &&
+             !(A.skip_null_writes && dst[p] == A.null_block);
+  }
+  bf16* out = static_cast<bf16*>(A.out);
+  const bf16* z = static_cast<const bf16*>(A.z);
+  if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
+    if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
+      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < n; ++p) store_bf16x4(out + (long long)(t0 + p) * A.ldo + h, zero);
+    return;
+  }
+  const bool src_ok = block_ok(src, A.inner_state);
+  if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+  float* st = static_cast<float*>(A.inner_state.data);
+  const long long cs = A.inner_state.col_stride;
+  const float* sp = st + (src_ok ? src : 0) * A.inner_state.block_stride + h;
+  // the snapshot stream's first loads go out before the short filter runs
+  float4 sv[U];
+#pragma unroll
+  for (int t = 0; t < U; ++t)
+    sv[t] = (src_ok && t < HIST) ? *reinterpret_cast<const float4*>(sp + (long long)t * cs)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+
+  // ---- short filter per column of the 4 channels' triples, window shift
+  const int W0 = A.conv_state.cols;
+  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const bf16* sw = static_cast<const bf16*>(P.short_w);
+  const bool write_conv = block_ok(cout, A.conv_state) &&
+                          !(A.skip_null_writes && cout == A.null_block);
+  float x2v[VQ][4], uv[VQ][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float xs[3][VQ];
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int col = 3 * (h + c) + q;
+      const float w0 = ldbf(sw + col * 3), w1 = ldbf(sw + col * 3 + 1), w2 = ldbf(sw + col * 3 + 2);
+      const bf16* wp = s0 + cin * A.conv_state.block_stride + col;
+      float c0 = off < W0 ? ldbf(wp + (long long)off * A.conv_state.col_stride) : 0.0f;
+      float c1 = off + 1 < W0 ? ldbf(wp + (long long)(off + 1) * A.conv_state.col_stride) : 0.0f;
+      float xz[VQ];
+#pragma unroll
+      for (int p = 0; p < VQ; ++p) {
+        xz[p] = 0.0f;
+        xs[q][p] = 0.0f;
+        if (p < n) {
+          xz[p] = ldbf(z + (long long)(t0 + p) * A.ldz + col);
+          xs[q][p] = short_tap(c0, c1, xz[p], w0, w1, w2);
+          c0 = c1;
+          c1 = xz[p];
+        }
+      }
+      if (write_conv) {
+        // column i <- old column off+1+i (read just before: in place, ascending
+        // i only overwrites columns already read) or the new inputs
+        const int val = W0 - n;
+        bf16* dp = s0 + cout * A.conv_state.block_stride + col;
+        for (int i = 0; i < W0; ++i) {
+          float v;
+          if (i < val) {
+            const int sc = off + 1 + i;
+            v = sc < W0 ? ldbf(wp + (long long)sc * A.conv_state.col_stride) : 0.0f;
+          } else {
+            v = pick(xz, i - val);
+          }
+          dp[(long long)i * A.conv_state.col_stride] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < VQ; ++p) {
+      x2v[p][c] = xs[0][p];
+      uv[p][c] = bf16r(xs[1][p] * xs[2][p]);
+    }
+  }
+
+  // ---- inner FIR over the accepted snapshot, verifier snapshots written
+  const bf16* w = static_cast<const bf16*>(P.inner_w) + h;  // (K, H), unit channel stride
+  const long long wk = P.inner_w_stride_k;
+  float y[VQ][4];
+#pragma unroll
+  for (int p = 0; p < VQ; ++p)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) y[p][c] = 0.0f;
+  float wr[VQ][4];  // wr[j] = weights of tap k - j
+#pragma unroll
+  for (int j = 0; j < VQ; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) wr[j][c] = 0.0f;
+  float* dbase[VQ];
+#pragma unroll
+  for (int p = 0; p < VQ; ++p) dbase[p] = st + (dok[p] ? dst[p] : 0) * A.inner_state.block_stride + h;
+#pragma unroll 1
+  for (int k0 = 0; k0 < HIST; k0 += U) {
+    float4 nx[U];
+#pragma unroll
+    for (int t = 0; t < U; ++t)
+      nx[t] = (src_ok && k0 + U + t < HIST)
+                  ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + U + t) * cs)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      const int k = k0 + t;
+      if (k < HIST) {
+#pragma unroll
+        for (int j = VQ - 1; j > 0; --j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) wr[j][c] = wr[j - 1][c];
+        load_bf16x4(w + (long long)k * wk, wr[0]);
+        const float sx[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
+#pragma unroll
+        for (int p = 0; p < VQ; ++p) {
+          if (p < n && k >= p) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) y[p][c] = fmaf(wr[p][c], sx[c], y[p][c]);
+          }
+          if (p < n && dok[p] && k - p - 1 >= 0)
+            *reinterpret_cast<float4*>(dbase[p] + (long long)(k - p - 1) * cs) = sv[t];
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < U; ++t) sv[t] = nx[t];
+  }
+  // the verified tokens themselves: newest taps, and the tail of each snapshot
+#pragma unroll
+  for (int p = 0; p < VQ; ++p) {
+    if (p < n) {
+#pragma unroll
+      for (int i = 0; i < VQ; ++i) {
+        if (i < p) {
+          float wv[4];
+          load_bf16x4(w + (long long)(HIST + i - p) * wk, wv);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) y[p][c] = fmaf(wv[c], uv[i][c], y[p][c]);
+        }
+      }
+      float wl[4];
+      load_bf16x4(w + (long long)HIST * wk, wl);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) y[p][c] = fmaf(wl[c], uv[p][c], y[p][c]);
+      if (dok[p]) {
+#pragma unroll
+        for (int m = 0; m < VQ; ++m)
+          if (m <= p)
+            *reinterpret_cast<float4*>(dbase[p] + (long long)(HIST - 1 - p + m) * cs) =
+                make_float4(uv[m][0], uv[m][1], uv[m][2], uv[m][3]);
+      }
+    }
+  }
+  // ---- output gate
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  if (Dg) load_bf16x4(Dg + h, d);
+#pragma unroll
+  for (int p = 0; p < VQ; ++p) {
+    if (p < n) {
+      float g[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float yy = bf16r(y[p][c]);
+        if (Dg) yy = bf16r(yy + bf16r(d[c] * uv[p][c]));
+        g[c] = bf16r(x2v[p][c] * yy);
+      }
+      store_bf16x4(out + (long long)(t0 + p) * A.ldo + h, g);
+    }
+  }
+}
+
+// The FIR verify path: up to VQ positions, unit channel strides, 16-byte rows.
+static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
+  if (P.kind != HYENA_KIND_FIR || A.q > VQ) return false;
+  if (A.conv_state.dim_stride != 1) return false;
+  if (!aligned_elems(A.out, A.ldo, 2, 8)) return false;
+  const hyena_state_view& s = A.inner_state;
+  if (s.dim_stride != 1 || P.inner_w_stride_h != 1 || (P.inner_w_stride_k * 2) % 8 != 0) return false;
+  if (!aligned_elems(P.inner_w, 0, 2, 8) || (P.D && !aligned_elems(P.D, 0, 2, 8))) return false;
+  return aligned_elems(s.data, s.block_stride, 4, 16) && (s.col_stride * 4) % 16 == 0 &&
+         P.H % 4 == 0;
+}
+
 int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaStream_t st) {
   if (A.conv_state.cols > DEC_MAXW0)
     return fail(HYENA_ERR_UNSUPPORTED, "conv window wider than 8 columns");
@@ -570,6 +792,14 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaS
       launch_kernel(decode_fir_q1_kernel<7>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_fir_q1_kernel<7>");
     }
+  }
+  if (fir_verify_ok(P, A) && (P.K == 128 || P.K == 7)) {
+    dim3 g(A.num_reqs, (P.H / 4 + FAST_THREADS - 1) / FAST_THREADS);
+    if (P.K == 128)
+      launch_kernel(decode_fir_verify_kernel<128>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
+    else
+      launch_kernel(decode_fir_verify_kernel<7>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
+    return check_launch("decode_fir_verify_kernel");
   }
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
   if (P.kind == HYENA_KIND_IIR) {
