@@ -22,6 +22,9 @@ timing reduction crosses ranks.
            the full-width triple on its contiguous slice of the 262144-token
            sequence (FIR layers with a K+1-row halo, the LI layer in two passes
            around one all-gather of (H, 16) slice states); strong scaling.
+  --workload hcm256  config 1: one HCM block at H=256 (GPU path + CPU port).
+  --workload model7b config 4: the full random-init 7B model scoring a bounded
+           sample of the Markov sequences (prefill tok/s, mean NLL).
 
 `--impl reference` times the reference algorithm's CPU implementation (the
 oracle port in oracle/, all host threads) on a bounded sample of the same
@@ -707,6 +710,109 @@ def run_cp40b(args, world, rank, device, dist_ok):
         print(json.dumps(line))
 
 
+
+def run_hcm256(args, device):
+    """Config 1: one HCM mixer block at H = 256 (bf16 in_proj), 2 x 1024 uniform
+    ACGT tokens through an N(0,1) 512 x 256 table; the B200 path, with the
+    reference algorithm's CPU port timed beside it (cpu_baseline)."""
+    from evo2_flash_b200 import HyenaFIRMixer, set_forward_metadata
+    from evo2_flash_b200.synthetic import mixer_tensors
+
+    Hs, B, L = 256, 2, 1024
+    cfg = SimpleNamespace(hidden_size=Hs, short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=False)
+    t = mixer_tensors("hcm", Hs, 128, 0, fp8=False)
+    m = HyenaFIRMixer(cfg, 0, prefix="cfg1", k_inner=128, device=device)
+    m.load_full_weights({k: v.to(device) for k, v in t.items()})
+    m.allocate_state(B + 1, device)
+    table = torch.randn(512, Hs, generator=torch.Generator().manual_seed(1))
+    toks = acgt_tokens(B * L, torch.Generator().manual_seed(0))
+    x = rmsnorm(table[toks]).to(device)
+    meta = prefill_meta([L] * B, list(range(1, B + 1)), device)
+
+    def step():
+        with set_forward_metadata(meta):
+            m(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    from oracle import hyena_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    po = O.MixerParams(H=Hs, kind="fir", k_inner=128, short_filter=t["short_filter"], conv=t["conv"],
+                       D=t["D"], log_poles=None, residues=None, in_proj_weight=t["in_proj.weight"],
+                       in_proj_scales=None, out_proj_weight=t["out_proj.weight"],
+                       out_proj_bias=t["out_proj.bias"])
+    xc, mc = x.cpu(), prefill_meta([L] * B, list(range(1, B + 1)), "cpu")
+    ts = []
+    for i in range(4):
+        states = [torch.zeros(B + 1, 2, 3 * Hs, dtype=torch.bfloat16), torch.zeros(B + 1, 127, Hs),
+                  torch.zeros(B + 1, Hs, 16)]
+        t0 = time.perf_counter()
+        O.mixer_forward(xc, po, mc, states)
+        if i:
+            ts.append(time.perf_counter() - t0)
+    cpu = B * L / statistics.median(ts)
+    line = {
+        "metric": METRIC + " (config 1: one HCM block, H=256)", "value": B * L / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded uniform ACGT, random-init weights)",
+        "config": {"workload": "config1: HCM mixer block, H=256, bf16, 2 x 1024 tokens",
+                   "hidden": Hs, "global_batch": B, "seq_len": L,
+                   "l2": "fits in L2 (launch-bound case)"},
+        "cpu_baseline": {"value": cpu, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": "the whole config (2 x 1024 tokens), median of 3"},
+    }
+    print(json.dumps(line))
+
+
+def run_model7b(args, device):
+    """Config 4: the full random-init StripedHyena2 7B (32 blocks, attention at
+    3/10/17/24/31, fp8 Hyena in_proj) scoring a bounded sample of the 64
+    order-3-Markov ACGT sequences (lengths U[1k, 32k], seeded): prefill tok/s
+    and mean per-token NLL (parity with the all-reference arm is a test)."""
+    from evo2_flash_b200.model import StripedHyena2, StripedHyena2Config
+    from evo2_flash_b200.synthetic import markov_acgt
+
+    lens = torch.randint(1024, 32769, (64,), generator=torch.Generator().manual_seed(3)).tolist()
+    seqs = markov_acgt(lens[:args.model_seqs], seed=3)
+    model = StripedHyena2(StripedHyena2Config.evo2_7b(), device=device)
+    model.load_tensors(model.random_tensors(0, gen_device=device))
+    ntok = sum(len(s) for s in seqs)
+    for _ in range(max(1, args.warmup - 2)):
+        model.score(seqs[:1], max_tokens_per_step=args.model_step_tokens)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    nll = model.score(seqs, max_tokens_per_step=args.model_step_tokens)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    line = {
+        "metric": METRIC + " (config 4: full random-init 7B, scoring prefill)",
+        "value": ntok / (ms * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": 1,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3/bf16",
+        "data": "synthetic (seeded order-3 Markov ACGT, random-init weights)",
+        "config": {"workload": "config4: StripedHyena2 7B scoring", "sequences": len(seqs),
+                   "tokens": ntok, "max_tokens_per_step": args.model_step_tokens,
+                   "attention": "torch SDPA (outside the mixer path)"},
+        "mean_nll": sum(nll) / len(nll),
+    }
+    print(json.dumps(line))
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -721,7 +827,11 @@ def main():
     ap.add_argument("--only", choices=["prefill", "decode"], default=None,
                     help="run one workload (small profiling cases)")
     ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per rank")
-    ap.add_argument("--workload", choices=["triple", "tp40b", "cp40b"], default="triple")
+    ap.add_argument("--workload", choices=["triple", "tp40b", "cp40b", "hcm256", "model7b"],
+                    default="triple")
+    ap.add_argument("--model-seqs", type=int, default=8, help="model7b: sequences scored")
+    ap.add_argument("--model-step-tokens", type=int, default=65536,
+                    help="model7b: packed tokens per prefill step")
     ap.add_argument("--tp-chunk", type=int, default=32768, help="tp40b prefill chunk (tokens)")
     ap.add_argument("--tp-decode-steps", type=int, default=256)
     ap.add_argument("--tp-reserve-sms", type=int, default=0,
@@ -769,6 +879,13 @@ def main():
             kw["pg_options"] = opts
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device, **kw)
 
+    if args.workload in ("hcm256", "model7b"):
+        if rank == 0:
+            (run_hcm256 if args.workload == "hcm256" else run_model7b)(args, device)
+        if dist_ok:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload in ("tp40b", "cp40b"):
         (run_tp40b if args.workload == "tp40b" else run_cp40b)(args, world, rank, device, dist_ok)
         if dist_ok:
@@ -790,8 +907,11 @@ def main():
     if args.only == "decode":  # decode-only profiling case
         dgen = torch.Generator().manual_seed(2 + rank)
         d_ms, _ = run_decode(layers, table, device, args.decode_steps, args.warmup, dgen)
+        v_ms = run_verify(layers, table, device, max(10, args.decode_steps // 4), args.warmup,
+                          torch.Generator().manual_seed(4 + rank))
         if rank == 0:
-            print(json.dumps({"decode_ms_per_step": d_ms, "decode_tok_per_s": DECODE_B / d_ms * 1e3}))
+            print(json.dumps({"decode_ms_per_step": d_ms, "decode_tok_per_s": DECODE_B / d_ms * 1e3,
+                              "verify_ms_per_step": v_ms}))
         return
 
     with KernelTimer(ops_mod, "gemm_e4m3") as gt:
