@@ -561,7 +561,7 @@ static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A
 constexpr int VQ = 4;
 
 template <int K>
-__global__ void __launch_bounds__(FAST_THREADS)
+__global__ void __launch_bounds__(FAST_THREADS, 4)
 decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   pdl_entry();
   constexpr int HIST = K - 1;
@@ -609,14 +609,62 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
   float* st = static_cast<float*>(A.inner_state.data);
   const long long cs = A.inner_state.col_stride;
   const float* sp = st + (src_ok ? src : 0) * A.inner_state.block_stride + h;
-  // the snapshot stream's first loads go out before the short filter runs
   float4 sv[U];
 #pragma unroll
   for (int t = 0; t < U; ++t)
     sv[t] = (src_ok && t < HIST) ? *reinterpret_cast<const float4*>(sp + (long long)t * cs)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 
-  // ---- short filter per column of the 4 channels' triples, window shift
+  // ---- inner FIR over the accepted snapshot, verifier snapshots written
+  const bf16* w = static_cast<const bf16*>(P.inner_w) + h;  // (K, H), unit channel stride
+  const long long wk = P.inner_w_stride_k;
+  float y[VQ][4];
+#pragma unroll
+  for (int p = 0; p < VQ; ++p)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) y[p][c] = 0.0f;
+  float wr[VQ][4];  // wr[j] = weights of tap k - j
+#pragma unroll
+  for (int j = 0; j < VQ; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) wr[j][c] = 0.0f;
+  float* dbase[VQ];
+#pragma unroll
+  for (int p = 0; p < VQ; ++p) dbase[p] = st + (dok[p] ? dst[p] : 0) * A.inner_state.block_stride + h;
+#pragma unroll 1
+  for (int k0 = 0; k0 < HIST; k0 += U) {
+    float4 nx[U];
+#pragma unroll
+    for (int t = 0; t < U; ++t)
+      nx[t] = (src_ok && k0 + U + t < HIST)
+                  ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + U + t) * cs)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int t = 0; t < U; ++t) {
+      const int k = k0 + t;
+      if (k < HIST) {
+#pragma unroll
+        for (int j = VQ - 1; j > 0; --j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) wr[j][c] = wr[j - 1][c];
+        load_bf16x4(w + (long long)k * wk, wr[0]);
+        const float sx[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
+#pragma unroll
+        for (int p = 0; p < VQ; ++p) {
+          if (p < n && k >= p) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) y[p][c] = fmaf(wr[p][c], sx[c], y[p][c]);
+          }
+          if (p < n && dok[p] && k - p - 1 >= 0)
+            *reinterpret_cast<float4*>(dbase[p] + (long long)(k - p - 1) * cs) = sv[t];
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < U; ++t) sv[t] = nx[t];
+  }
+  // ---- short filter per column of the 4 channels' triples, window shift (after
+  // the stream, so that its values are not held in registers across it)
   const int W0 = A.conv_state.cols;
   bf16* s0 = static_cast<bf16*>(A.conv_state.data);
   const bf16* sw = static_cast<const bf16*>(P.short_w);
@@ -669,54 +717,6 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
     }
   }
 
-  // ---- inner FIR over the accepted snapshot, verifier snapshots written
-  const bf16* w = static_cast<const bf16*>(P.inner_w) + h;  // (K, H), unit channel stride
-  const long long wk = P.inner_w_stride_k;
-  float y[VQ][4];
-#pragma unroll
-  for (int p = 0; p < VQ; ++p)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) y[p][c] = 0.0f;
-  float wr[VQ][4];  // wr[j] = weights of tap k - j
-#pragma unroll
-  for (int j = 0; j < VQ; ++j)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) wr[j][c] = 0.0f;
-  float* dbase[VQ];
-#pragma unroll
-  for (int p = 0; p < VQ; ++p) dbase[p] = st + (dok[p] ? dst[p] : 0) * A.inner_state.block_stride + h;
-#pragma unroll 1
-  for (int k0 = 0; k0 < HIST; k0 += U) {
-    float4 nx[U];
-#pragma unroll
-    for (int t = 0; t < U; ++t)
-      nx[t] = (src_ok && k0 + U + t < HIST)
-                  ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + U + t) * cs)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int t = 0; t < U; ++t) {
-      const int k = k0 + t;
-      if (k < HIST) {
-#pragma unroll
-        for (int j = VQ - 1; j > 0; --j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) wr[j][c] = wr[j - 1][c];
-        load_bf16x4(w + (long long)k * wk, wr[0]);
-        const float sx[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
-#pragma unroll
-        for (int p = 0; p < VQ; ++p) {
-          if (p < n && k >= p) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) y[p][c] = fmaf(wr[p][c], sx[c], y[p][c]);
-          }
-          if (p < n && dok[p] && k - p - 1 >= 0)
-            *reinterpret_cast<float4*>(dbase[p] + (long long)(k - p - 1) * cs) = sv[t];
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < U; ++t) sv[t] = nx[t];
-  }
   // the verified tokens themselves: newest taps, and the tail of each snapshot
 #pragma unroll
   for (int p = 0; p < VQ; ++p) {
