@@ -157,7 +157,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -290,24 +290,47 @@ def run_prefill(layers, x, meta, steps, warmup, dist_ok, device, gemm_timer):
 
 
 def run_e2e(layers, x_host, meta, steps, device):
-    """Public-API end to end: pinned host hidden states -> device, the triple, the
-    last layer's output back to pinned host memory, every step."""
+    """Public-API end to end: every step copies the hidden states from pinned host
+    memory to the device, runs the triple, and copies the last layer's output
+    back to pinned host memory.  The copies run on their own streams (one per
+    direction), double-buffered, so step i+1's upload and step i-1's download
+    overlap step i's kernels; the timed region spans the first upload to the last
+    download."""
     from evo2_flash_b200 import set_forward_metadata
 
-    out_host = torch.empty_like(x_host, pin_memory=True)
+    comp = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    xbuf = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
+    out_host = [torch.empty_like(x_host, pin_memory=True) for _ in range(2)]
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        x = x_host.to(device, non_blocking=True)
+    e0.record(up)
+    with torch.cuda.stream(up):
+        xbuf[0].copy_(x_host, non_blocking=True)
+        uploaded[0].record(up)
+    for i in range(steps):
+        b = i % 2
+        comp.wait_event(uploaded[b])
         with set_forward_metadata(meta):
             for m, _ in layers:
-                y = m(x)
-        out_host.copy_(y, non_blocking=True)
-    e1.record()
+                y = m(xbuf[b])
+        computed[b].record(comp)
+        if i + 1 < steps:
+            with torch.cuda.stream(up):
+                if i >= 1:
+                    up.wait_event(computed[1 - b])  # step i-1 no longer reads that buffer
+                xbuf[1 - b].copy_(x_host, non_blocking=True)
+                uploaded[1 - b].record(up)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[b])
+            y.record_stream(down)
+            out_host[b].copy_(y, non_blocking=True)
+    down.wait_stream(up)
+    e1.record(down)
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1), x_host.numel() * x_host.element_size(), out_host.numel() * 2
+    return e0.elapsed_time(e1), x_host.numel() * x_host.element_size(), out_host[0].numel() * 2
 
 
 def run_decode(layers, table, device, steps, warmup, gen):
@@ -817,7 +840,7 @@ def run_model7b(args, device):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--decode-steps", type=int, default=200)
@@ -966,8 +989,9 @@ def main():
     e2e = None
     if not args.no_e2e:
         x_host = x.cpu().pin_memory()
-        e_ms, h2d, d2h = run_e2e(layers, x_host, meta, max(2, args.steps // 2), device)
-        e_step = e_ms / max(2, args.steps // 2)
+        e_steps = max(3, args.steps)
+        e_ms, h2d, d2h = run_e2e(layers, x_host, meta, e_steps, device)
+        e_step = e_ms / e_steps
         if dist_ok:
             tt = torch.tensor([e_step], device=device)
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
