@@ -39,6 +39,14 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
                      size_t ws_bytes, cudaStream_t st);
 size_t gemm_workspace_size(int M, int N, int K, bool fp8);
 void gemm_set_max_ctas(int n);
+int spec_accepted_launch(const int32_t* slots, int64_t slot_stride, int num_reqs,
+                         const int32_t* computed, const float* stamps, int64_t stamp_stride,
+                         int num_blocks, int num_spec, int32_t* accepted, int32_t* error_flags,
+                         cudaStream_t st);
+int spec_record_launch(const int32_t* out_slots, int64_t s0, int64_t s1, int num_reqs, int q,
+                       const int32_t* starts, const int32_t* computed, float* stamps,
+                       int64_t stamp_stride, int num_blocks, int32_t* error_flags,
+                       cudaStream_t st);
 
 static int check_params(const hyena_layer_params* p) {
   HB_REQUIRE(p != nullptr, "null layer params");
@@ -73,6 +81,24 @@ extern "C" {
 int hyena_abi_version(void) { return HYENA_ABI_VERSION; }
 
 void hyena_set_gemm_max_ctas(int32_t n) { hb::gemm_set_max_ctas(n); }
+
+int hyena_spec_accepted(const int32_t* slots, int64_t slot_stride, int32_t num_reqs,
+                        const int32_t* computed, const float* stamps, int64_t stamp_stride,
+                        int32_t num_blocks, int32_t num_spec, int32_t* accepted,
+                        int32_t* error_flags, void* stream) {
+  return hb::spec_accepted_launch(slots, slot_stride, num_reqs, computed, stamps, stamp_stride,
+                                  num_blocks, num_spec, accepted, error_flags,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int hyena_spec_record(const int32_t* out_slots, int64_t s0, int64_t s1, int32_t num_reqs,
+                      int32_t q, const int32_t* starts, const int32_t* computed, float* stamps,
+                      int64_t stamp_stride, int32_t num_blocks, int32_t* error_flags,
+                      void* stream) {
+  return hb::spec_record_launch(out_slots, s0, s1, num_reqs, q, starts, computed, stamps,
+                                stamp_stride, num_blocks, error_flags,
+                                static_cast<cudaStream_t>(stream));
+}
 
 void hyena_set_launch_chaining(int32_t enable) {
   hb::g_launch_chaining.store(enable != 0, std::memory_order_relaxed);

@@ -95,8 +95,9 @@ def _accepted_tokens(m, num_reqs, device):
 
 
 def _decode_tensors(m, num_tokens, max_positions=None, accepted=None):
-    """(in_slots, out_slots, starts, ends, accepted) on device (mixers.py:459-524),
-    including the prefix-caching ("all" mode) slot gathers (mixers.py:443-456)."""
+    """(in_slots, out_slots, starts, accepted) on device (mixers.py:459-524),
+    including the prefix-caching ("all" mode) slot gathers (mixers.py:443-456).
+    accepted=False skips the accepted counts (returned as None)."""
     slots = m.state_indices_tensor_d
     if slots.dim() == 1:
         slots = slots[:, None]
@@ -116,10 +117,12 @@ def _decode_tensors(m, num_tokens, max_positions=None, accepted=None):
             raise ValueError(f"query_start_loc_d is too short: shape={tuple(starts.shape)}, "
                              f"num_decodes={num_reqs}")
         starts = starts[: num_reqs + 1]
-    if accepted is None:
+    if accepted is False:  # the caller needs the slots only
+        accepted = None
+    elif accepted is None:
         accepted = _accepted_tokens(m, num_reqs, slots.device)
     else:
-        accepted = accepted[:num_reqs].to(torch.long)
+        accepted = accepted[:num_reqs]
     slots = slots[:num_reqs]
     previous = getattr(m, "block_idx_last_scheduled_token_prev_step", None)
     scheduled = getattr(m, "block_idx_last_scheduled_token", None)
@@ -227,6 +230,10 @@ class HyenaMixerBase(nn.Module):
         return self.kv_cache[2][:, 0, -1]
 
     def _spec_accepted(self, m):
+        """Accepted tokens per request from the position stamps (mixers.py:962-984),
+        in one kernel (hyena_spec_accepted).  A mismatching stamp, where the
+        reference's device assert fires, is clamped and reported through the
+        kernel's error word instead."""
         nd = int(m.num_decodes)
         computed = getattr(m, "num_computed_tokens_d", None)
         if computed is None:
@@ -235,11 +242,8 @@ class HyenaMixerBase(nn.Module):
         slots = m.state_indices_tensor_d[:nd]
         if slots.dim() == 1:
             slots = slots[:, None]
-        first = _cache_safe_state_indices(slots, self.kv_cache[2])[:, 0].long()
-        offset = computed[:nd].to(torch.int64) - self._position_stamps()[first].to(torch.int64)
-        torch._assert_async(((first == 0) | ((offset >= 0) & (offset <= self.num_spec))).all(),
-                            "Evo 2 speculative state stamp does not match the request position")
-        return offset.clamp(0, self.num_spec) + 1
+        slots = _cache_safe_state_indices(slots, self.kv_cache[2])
+        return ops.spec_accepted(slots, computed[:nd], self._position_stamps(), self.num_spec)
 
     def _repair_resumed_prefill_state(self, m):
         if not self.num_spec or not int(m.num_prefills):
@@ -266,21 +270,17 @@ class HyenaMixerBase(nn.Module):
         return None
 
     def _record_stamps(self, m):
+        """Stamps of the slots written this step (mixers.py:1040-1074): verifier
+        slots in one kernel (hyena_spec_record), prefill blocks in torch."""
         if not self.num_spec:
             return
         stamps = self._position_stamps()
         nd = int(m.num_decodes)
         if nd and self.is_speculative_decode(m):
-            ones = torch.ones(nd, device=stamps.device, dtype=torch.long)
-            _, outs, starts, _ = _decode_tensors(m, int(m.num_decode_tokens), 1 + self.num_spec, ones)
+            _, outs, starts, _ = _decode_tensors(m, int(m.num_decode_tokens), 1 + self.num_spec,
+                                                 accepted=False)
             outs = _cache_safe_state_indices(outs, self.kv_cache[2])
-            steps = torch.arange(outs.shape[1], device=outs.device)
-            lens = (starts[1:] - starts[:-1]).long()
-            active = steps[None, :] < lens[:, None]
-            computed = m.num_computed_tokens_d[:nd].to(torch.int64)
-            values = computed[:, None] + steps[None, :] + 1
-            dest = torch.where(active, outs.long(), 0).reshape(-1)
-            stamps.index_put_((dest,), torch.where(active, values, 0).reshape(-1).to(stamps.dtype))
+            ops.spec_record(outs, starts, m.num_computed_tokens_d[:nd], stamps)
         npf = int(m.num_prefills)
         if npf:
             stamps[m.state_indices_tensor_p[:npf].long()] = m.seq_lens[nd:nd + npf].to(stamps.dtype)

@@ -270,6 +270,44 @@ def set_gemm_max_ctas(n: int) -> None:
     _lib.load().hyena_set_gemm_max_ctas(int(n))
 
 
+def _stamp_view(stamps):
+    """(base pointer, element stride) of a 1-D fp32 stamp view (one per block)."""
+    _require(stamps.dim() == 1 and stamps.dtype == torch.float32, "stamps must be a 1-D fp32 view")
+    return stamps.data_ptr(), stamps.stride(0)
+
+
+def spec_accepted(slots, computed, stamps, num_spec, out=None, error_flags=None):
+    """accepted (R,) int32 = clamp(computed - stamp(slots[:, 0]), 0, num_spec) + 1
+    (hyena_spec_accepted; mixers.py:962-984).  slots (R,) or (R, S) int32."""
+    lib = _lib.load()
+    first = slots if slots.dim() == 1 else slots[:, 0]
+    first = _i32(first, "slots")
+    comp = _i32(computed[: first.shape[0]].contiguous(), "computed")
+    R = first.shape[0]
+    if out is None:
+        out = torch.empty(R, dtype=torch.int32, device=first.device)
+    base, stride = _stamp_view(stamps)
+    _lib.check(lib.hyena_spec_accepted(first.data_ptr(), first.stride(0) if R else 1, R,
+                                       comp.data_ptr(), base, stride, stamps.shape[0], int(num_spec),
+                                       out.data_ptr(), _ptr(error_flags), _stream()),
+               "hyena_spec_accepted")
+    return out
+
+
+def spec_record(out_slots, starts, computed, stamps, error_flags=None):
+    """stamp(out_slots[r, p]) = computed[r] + p + 1 for the active positions p of
+    each request (hyena_spec_record; mixers.py:1040-1062)."""
+    lib = _lib.load()
+    slots = _i32(out_slots if out_slots.dim() == 2 else out_slots[:, None], "out_slots")
+    R, q = slots.shape
+    st = _i32(starts[: R + 1].contiguous(), "starts")
+    comp = _i32(computed[:R].contiguous(), "computed")
+    base, stride = _stamp_view(stamps)
+    _lib.check(lib.hyena_spec_record(slots.data_ptr(), slots.stride(0), slots.stride(1), R, q,
+                                     st.data_ptr(), comp.data_ptr(), base, stride, stamps.shape[0],
+                                     _ptr(error_flags), _stream()), "hyena_spec_record")
+
+
 def set_launch_chaining(enable: bool) -> None:
     """Programmatic dependent launch between this library's kernels on/off
     (hyena_set_launch_chaining; on by default)."""

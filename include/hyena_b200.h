@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define HYENA_ABI_VERSION 2
+#define HYENA_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define HYENA_API __attribute__((visibility("default")))
@@ -46,6 +46,7 @@ extern "C" {
 /* Bits OR-ed into *error_flags by the kernels. */
 #define HYENA_FLAG_BLOCK_RANGE 1 /* a state block index was outside [0, num_blocks) */
 #define HYENA_FLAG_SEGMENT 2     /* query_start_loc was not non-decreasing / exceeded T */
+#define HYENA_FLAG_STAMP 4       /* a position stamp did not match the request position */
 
 typedef struct hyena_state_view {
   void* data;            /* element (block 0, column 0, channel 0) */
@@ -194,6 +195,31 @@ HYENA_API int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t
 /* Bytes of workspace the GEMMs above use at this shape: always 0 (kept so that
  * callers written against ABI version 2 keep working).  fp8 != 0 selects e4m3. */
 HYENA_API size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8);
+
+/* ---------------------------------------------------------------- speculative bookkeeping
+ * Position stamps: one fp32 per state block at stamps + block * stamp_stride
+ * (the last column of S2's first channel, mixers.py:952-957).
+ *
+ * Accepted token count per request from the stamps, replacing _spec_accepted
+ * (mixers.py:962-984): first = slots[r * slot_stride]; offset = computed[r] -
+ * stamp(first); accepted[r] = clamp(offset, 0, num_spec) + 1 (int32).  Where the
+ * reference's device assert would fire (a non-null first slot with offset
+ * outside [0, num_spec]) HYENA_FLAG_STAMP is set in *error_flags instead; a
+ * first slot outside [0, num_blocks) sets HYENA_FLAG_BLOCK_RANGE (accepted 1). */
+HYENA_API int hyena_spec_accepted(const int32_t* slots, int64_t slot_stride, int32_t num_reqs,
+                                  const int32_t* computed, const float* stamps,
+                                  int64_t stamp_stride, int32_t num_blocks, int32_t num_spec,
+                                  int32_t* accepted, int32_t* error_flags, void* stream);
+
+/* Stamps of the verifier slots after a decode / verify step, replacing the
+ * decode half of _record_stamps (mixers.py:1040-1062): for p < min(q, starts[r+1]
+ * - starts[r]), stamp(out_slots[r * s0 + p * s1]) = computed[r] + p + 1.  Block 0
+ * (the null block, whose stamp is never consulted) is not written; the
+ * reference writes 0 there for inactive positions. */
+HYENA_API int hyena_spec_record(const int32_t* out_slots, int64_t s0, int64_t s1, int32_t num_reqs,
+                                int32_t q, const int32_t* starts, const int32_t* computed,
+                                float* stamps, int64_t stamp_stride, int32_t num_blocks,
+                                int32_t* error_flags, void* stream);
 
 /* Caps the CTAs of the persistent (large-M) GEMMs at n (n <= 0: one per SM,
  * the default).  Process-wide.  A caller that overlaps GEMMs with collectives

@@ -328,3 +328,47 @@ def test_small_m_gemm_cluster_split_k_is_deterministic(fp8, M):
     torch.cuda.synchronize()
     assert max_rel_err(first, ref) < 1e-2
     assert torch.equal(first, second)
+
+
+def test_spec_bookkeeping_matches_the_stamp_rules():
+    """hyena_spec_accepted / hyena_spec_record against the reference's torch
+    rules (mixers.py:962-984, 1040-1062) on random stamps: accepted = clamp(
+    computed - stamp(first slot), 0, num_spec) + 1; stamps of the active verifier
+    slots = computed + p + 1; a mismatching non-null stamp sets the flag."""
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(91)
+    nb, R, q, ns = 64, 9, 4, 3
+    s2 = torch.zeros(nb, 8, 17)
+    s2[:, 0, 16] = torch.randint(0, 1000, (nb,), generator=g).float()
+    slots = torch.randperm(nb - 1, generator=g)[: R * q].add(1).view(R, q).int()
+    slots[2, 0] = 0  # a null first slot
+    stamp_first = s2[slots[:, 0].long(), 0, 16]
+    offs = torch.randint(0, ns + 1, (R,), generator=g)
+    computed = (stamp_first + offs).int()
+    ds2 = s2.to(DEV)
+    stamps = ds2[:, 0, 16]
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    acc = ops.spec_accepted(slots.to(DEV), computed.to(DEV), stamps, ns, error_flags=flags)
+    want = (computed.long() - stamp_first.long()).clamp(0, ns) + 1
+    torch.cuda.synchronize()
+    assert torch.equal(acc.cpu().long(), want)
+    assert int(flags.item()) == 0
+    bad = computed.clone()
+    bad[0] += 50  # offset beyond num_spec on a non-null slot
+    ops.spec_accepted(slots.to(DEV), bad.to(DEV), stamps, ns, error_flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) & 4
+
+    lens = torch.tensor([4, 2, 1, 3, 4, 1, 2, 4, 3])
+    starts = torch.cat([torch.zeros(1, dtype=torch.long), lens.cumsum(0)]).int()
+    ops.spec_record(slots.to(DEV), starts.to(DEV), computed.to(DEV), stamps)
+    ref = s2[:, 0, 16].clone()
+    for r in range(R):
+        for p in range(int(lens[r])):
+            b = int(slots[r, p])
+            if b:
+                ref[b] = float(int(computed[r]) + p + 1)
+    torch.cuda.synchronize()
+    got = ds2[:, 0, 16].cpu()
+    assert torch.equal(got[1:], ref[1:])
