@@ -259,11 +259,14 @@ def test_quant_e4m3_exact():
 
     g = torch.Generator().manual_seed(71)
     x = (torch.randn(300, 512, generator=g) * 3).to(torch.bfloat16)
+    x[0, :6] = torch.tensor([float("inf"), -float("inf"), float("nan"), 0.0, -0.0, 4.48])
     sx = torch.tensor([0.01], dtype=torch.float32)
     ref = O.quantize_input(x, sx)
     q = ops.quant_e4m3(x.to(DEV), sx.to(DEV))
     torch.cuda.synchronize()
-    assert torch.equal(q.float().cpu(), ref)
+    got = q.float().cpu()
+    assert torch.equal(torch.isnan(got), torch.isnan(ref))  # NaN stays NaN, as torch's clamp
+    assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(ref))
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
