@@ -28,14 +28,22 @@ constexpr int FIR_RING = 256;    // u ring rows (power of two >= K-1 + FIR_BT)
 constexpr int FIR_WORDS = 3 * FIR_PAIRS;  // bf16x2 words of z per row per CTA
 constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
 
+// z tiles in flight per CTA (one being consumed, the rest loading).  Three
+// stages for K = 7 measured no faster than two (the kernel is not bound by
+// bytes in flight), so both kernels use two.
+template <int K>
+__host__ __device__ constexpr int fir_stages() {
+  return 2;
+}
+
 // Thread (pair p = tid % 16, row group g = tid / 16) owns channels c0+2p, c0+2p+1
-// and tile rows 8g .. 8g+7 in both the gate and the tap phases.
+// and tile rows 8g .. 8g+7 in both the gate and the tap phases (so the x2 it
+// gates with stays in its registers).
 template <int K>
 struct FirShared {
-  f2 ring[FIR_RING][FIR_PAIRS];          // u by row (mod FIR_RING), fp32 pairs
-  uint32_t zt[2][FIR_BT][FIR_WORDS];     // z tiles (double buffered), raw bf16x2 words
-  bf162 x2s[FIR_BT][FIR_PAIRS];          // x2 of the tile
-  f2 wsm[K][FIR_PAIRS];                  // inner taps as fp32 pairs, [k][pair]
+  f2 ring[FIR_RING][FIR_PAIRS];                   // u by row (mod FIR_RING), fp32 pairs
+  uint32_t zt[fir_stages<K>()][FIR_BT][FIR_WORDS];  // z tiles (multi-buffered), bf16x2 words
+  f2 wsm[K][FIR_PAIRS];                           // inner taps as fp32 pairs, [k][pair]
   uint32_t zh[2][FIR_WORDS];             // z rows (r-2, r-1) before the tile
   bf162 sw[3][3][FIR_PAIRS];             // short taps [column x2/x1/v][tap][pair]
   bf162 dsm[FIR_PAIRS];
@@ -127,6 +135,8 @@ __device__ __forceinline__ TileIt tile_at(const hyena_prefill_args& A, int r, in
   return t;
 }
 
+// Issues tile t's z rows into buffer buf and closes one cp.async group (empty
+// when t.n == 0, so that every loop iteration commits exactly one group).
 template <int K>
 __device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefill_args& A,
                                               const TileIt& t, int buf, int c0) {
@@ -164,9 +174,16 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float* s1 = static_cast<const float*>(A.inner_state.data);
 
+  constexpr int NST = fir_stages<K>();
   TileIt t = tile_at(A, r0, r1, find_segment(qsl, nseg, r0));
   int buf = 0;
-  if (t.n > 0) prefetch_tile(S, A, t, buf, c0);
+  TileIt pf = t;  // the last tile put in flight
+  prefetch_tile(S, A, pf, 0, c0);
+#pragma unroll
+  for (int s = 1; s < NST - 1; ++s) {
+    pf = tile_at(A, pf.r + pf.n, r1, pf.j);
+    prefetch_tile(S, A, pf, s, c0);
+  }
 
   for (int i = tid; i < K * FIR_PAIRS; i += FIR_THREADS) {
     const int k = i / FIR_PAIRS, pp = i % FIR_PAIRS;
@@ -192,7 +209,9 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
 
   while (t.n > 0) {
     const TileIt nt = tile_at(A, t.r + t.n, r1, t.j);
-    if (nt.n > 0) prefetch_tile(S, A, nt, buf ^ 1, c0);
+    // the tile NST-1 ahead goes into the buffer the previous tile has released
+    pf = tile_at(A, pf.r + pf.n, r1, pf.j);
+    prefetch_tile(S, A, pf, (buf + NST - 1) % NST, c0);
 
     if (t.j != cur_seg) {
       // ---- new segment (or the CTA's first rows): history rows [r-HIST, r) and z rows r-2, r-1
@@ -227,12 +246,13 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         S.zh[q][wd] = lo | (hi << 16);
       }
     }
-    if (nt.n > 0) cp_async_wait<1>(); else cp_async_wait<0>();
+    cp_async_wait<NST - 1>();  // this tile's group (one group is committed per tile)
     __syncthreads();
 
     const int n = t.n, r = t.r;
     // ---- K=3 short filter on channel pairs, sliding over 8 consecutive rows
     const int g0 = rg * FIR_RPT;
+    bf162 x2r[FIR_RPT];
     if (g0 < n) {
       bf162 w[3][3];
 #pragma unroll
@@ -260,7 +280,7 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
             h1[c] = cur[c];
           }
           S.ring[(r + row) & (FIR_RING - 1)][pp] = f2_from_bf162(__hmul2(o[1], o[2]));
-          S.x2s[row][pp] = o[0];
+          x2r[i] = o[0];
         }
       }
     }
@@ -317,12 +337,12 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
           bf162 y = bf162_from_f2(acc[q]);
           if (has_d)
             y = __hadd2(y, __hmul2(d2, bf162_from_f2(S.ring[(r + i0 + q) & (FIR_RING - 1)][pp])));
-          outp[q * ld2] = __hmul2(S.x2s[i0 + q][pp], y);
+          outp[q * ld2] = __hmul2(x2r[q], y);
         }
       }
     }
     __syncthreads();
-    buf ^= 1;
+    buf = (buf + 1) % NST;
     t = nt;
   }
 }
