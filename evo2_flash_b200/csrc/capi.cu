@@ -1,5 +1,6 @@
 // C ABI entry points: argument validation, dispatch, thread-local error text.
 #include <atomic>
+#include <cmath>
 #include <cstdio>
 
 #include "common.cuh"
@@ -172,6 +173,19 @@ int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void
   HB_REQUIRE(A && B && out, "null gemm pointer");
   return gemm_bf16_launch(A, lda, B, ldb, out, ldo, M, N, K, bias, workspace, workspace_bytes,
                           static_cast<cudaStream_t>(stream));
+}
+
+int hyena_rms_norm(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                   const void* weight, float eps, void* s_out, int64_t lds, void* y, int64_t ldy,
+                   void* q, int64_t ldq, const float* input_scale, int32_t M, int32_t H,
+                   void* stream) {
+  HB_REQUIRE(M >= 0, "rms_norm: negative row count");
+  hb::NormArgs A{static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(residual), ldr,
+                 static_cast<const bf16*>(weight), static_cast<bf16*>(s_out), lds,
+                 static_cast<bf16*>(y), ldy, static_cast<uint8_t*>(q), ldq, input_scale, M, H,
+                 // H ** -0.5 as a Python float, then the fp32 scalar torch multiplies by
+                 static_cast<float>(std::pow(static_cast<double>(H), -0.5)), eps};
+  return hb::rms_norm_launch(A, static_cast<cudaStream_t>(stream));
 }
 
 size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8) {

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -17,6 +18,26 @@ typedef __nv_bfloat16 bf16;
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int check_launch(const char* what);
+
+// Arguments of the decoder-layer norm (hyena_rms_norm).
+struct NormArgs {
+  const bf16* x;
+  int64_t ldx;
+  const bf16* r;  // residual or null
+  int64_t ldr;
+  const bf16* w;  // (H)
+  bf16* s;        // x + r, or null
+  int64_t lds;
+  bf16* y;        // normed output, or null
+  int64_t ldy;
+  uint8_t* q;     // e4m3 output, or null
+  int64_t ldq;
+  const float* sx;  // e4m3 input scale (q only)
+  int M, H;
+  float inv_sqrt_h, eps;
+};
+
+int rms_norm_launch(const NormArgs& A, cudaStream_t st);
 
 #define HB_REQUIRE(cond, msg)                                    \
   do {                                                           \
@@ -82,6 +103,61 @@ __device__ __forceinline__ float bf16r(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 __device__ __forceinline__ float ldbf(const bf16* p) { return __bfloat162float(*p); }
+
+// ---------------------------------------------------------------- quotients
+// A divide by a per-row or per-tensor divisor b whose fp32 quotient is then
+// rounded to a narrow type (bf16 or e4m3), with the result of the correctly
+// rounded __fdiv_rn but mostly without its cost.  rb = __frcp_rn(b); for b in
+// [2^-125, 2^125] and |a / b| in [2^-100, 2^100], p = fl(a * rb) differs from
+// a / b by at most 2^-23 |a / b| (two roundings of relative error 2^-24 each),
+// so p lies within 3 ulps of fl(a / b) in its binade, within 6 fp32 encodings
+// across a binade edge.  Rounding to the narrow type is monotonic, so when the
+// encodings 8 below and 8 above p convert to the same value, fl(a / b) does
+// too; otherwise (p near a rounding tie, or out of range) the quotient is
+// recomputed with __fdiv_rn.  a = 0 gives an exact p = +-0.
+__device__ __forceinline__ bool quot_divisor_ok(float b) {
+  const float m = fabsf(b);
+  return m >= 0x1p-125f && m <= 0x1p125f;
+}
+__device__ __forceinline__ bool quot_in_range(float p) {
+  const float m = fabsf(p);
+  return m >= 0x1p-100f && m <= 0x1p100f;
+}
+// a / b rounded to bf16 (returned as fp32).
+__device__ __forceinline__ float quot_bf16(float a, float b, float rb, bool fast) {
+  if (fast) {
+    const float p = a * rb;
+    if (a == 0.0f) return p;
+    if (quot_in_range(p)) {
+      const uint32_t u = __float_as_uint(p);
+      const float lo = bf16r(__uint_as_float(u - 8u)), hi = bf16r(__uint_as_float(u + 8u));
+      if (lo == hi) return lo;
+    }
+  }
+  return bf16r(__fdiv_rn(a, b));
+}
+// (a0, a1) / b as a saturating e4m3 pair: clamp to +-448 then round to nearest
+// even (NaN stays NaN), the quantisation of fp8_emul.quantize_input
+// (fp8_emul.py:76-78).
+__device__ __forceinline__ __nv_fp8x2_storage_t e4m3x2(float x0, float x1) {
+  return __nv_cvt_float2_to_fp8x2(make_float2(x0, x1), __NV_SATFINITE, __NV_E4M3);
+}
+__device__ __forceinline__ __nv_fp8x2_storage_t quot_e4m3x2(float a0, float a1, float b, float rb,
+                                                             bool fast) {
+  if (fast) {
+    const float p0 = a0 * rb, p1 = a1 * rb;
+    const bool z0 = a0 == 0.0f, z1 = a1 == 0.0f;
+    if ((z0 || quot_in_range(p0)) && (z1 || quot_in_range(p1))) {
+      const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
+      const __nv_fp8x2_storage_t lo = e4m3x2(z0 ? p0 : __uint_as_float(u0 - 8u),
+                                             z1 ? p1 : __uint_as_float(u1 - 8u));
+      const __nv_fp8x2_storage_t hi = e4m3x2(z0 ? p0 : __uint_as_float(u0 + 8u),
+                                             z1 ? p1 : __uint_as_float(u1 + 8u));
+      if (lo == hi) return lo;
+    }
+  }
+  return e4m3x2(__fdiv_rn(a0, b), __fdiv_rn(a1, b));
+}
 
 // Multiply and add with separate roundings (no FMA contraction): the order of
 // an eager torch recurrence s = s * p + x.

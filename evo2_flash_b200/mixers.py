@@ -141,6 +141,7 @@ class HyenaMixerBase(nn.Module):
     """Shared front half: in_proj -> stateful K=3 FIR -> de-interleave -> gate."""
 
     kind = "fir"
+    fuses_pre_norm = True  # forward() takes pre_norm= / residual=
 
     def __init__(self, config, layer_idx: int, model_config=None, cache_config=None,
                  prefix: str = "", quant_config=None, *, num_spec: int | None = None,
@@ -286,7 +287,19 @@ class HyenaMixerBase(nn.Module):
             stamps[m.state_indices_tensor_p[:npf].long()] = m.seq_lens[nd:nd + npf].to(stamps.dtype)
 
     # ---- forward ----------------------------------------------------------------
-    def _project(self, hidden_states, token_ids=None):
+    def _project(self, hidden_states, token_ids=None, pre_norm=None, residual=None):
+        if pre_norm is not None:
+            # The decoder layer's pre-norm (and residual add) in the in_proj's input
+            # pass: with the fp8 projection and no hook on it, the normed input
+            # only ever exists as e4m3 (ops.rms_norm).
+            ip = self.in_proj
+            fused = isinstance(ip, Fp8InProj) and not (ip._forward_hooks or ip._forward_pre_hooks)
+            y, q = ops.rms_norm(hidden_states, pre_norm.weight, pre_norm.eps, residual,
+                                want_y=not fused, quant_scale=ip.input_scale if fused else None,
+                                s_out=residual)
+            if fused:
+                return ops.gemm_e4m3(q, ip.weight, ip.input_scale, ip.weight_scale)
+            hidden_states = y
         z, _ = self.in_proj(hidden_states)
         return z
 
@@ -339,15 +352,19 @@ class HyenaMixerBase(nn.Module):
             return PendingReduce(out, None, None, finish)
         return out
 
-    def _forward_impl(self, hidden_states, token_ids=None, async_reduce=False):
+    def _forward_impl(self, hidden_states, token_ids=None, async_reduce=False, pre_norm=None,
+                      residual=None):
+        if residual is not None and pre_norm is None:
+            raise ValueError("residual is added inside the pre-norm: pass pre_norm too")
         m = self._meta()
         if m is None:
-            out = self._profile_run(hidden_states, token_ids)
+            out = self._profile_run(hidden_states, token_ids, pre_norm, residual)
             return PendingReduce(out, None, None) if async_reduce else out
         self._repair_resumed_prefill_state(m)
         accepted = self._resolve_accepted(m)  # before any state is written
         nd, npt = int(m.num_decode_tokens), int(m.num_prefill_tokens)
-        z = self._project(hidden_states[: nd + npt], token_ids)
+        z = self._project(hidden_states[: nd + npt], token_ids, pre_norm,
+                          None if residual is None else residual[: nd + npt])
         g = self._run_core(z, m, accepted)
         self._record_stamps(m)
         finish = lambda out: self._unpad(out, hidden_states, nd + npt)  # noqa: E731
@@ -355,15 +372,23 @@ class HyenaMixerBase(nn.Module):
             return self._out_proj(g, True, finish)
         return finish(self._out_proj(g))
 
-    def forward(self, hidden_states, token_ids=None):
-        return self._forward_impl(hidden_states, token_ids)
+    def forward(self, hidden_states, token_ids=None, *, pre_norm=None, residual=None):
+        """(T, H) bf16 -> (T, H) bf16 (mixers.py:823-829).
 
-    def forward_async(self, hidden_states, token_ids=None) -> PendingReduce:
+        With `pre_norm` (the decoder layer's Evo2RMSNorm: `.weight`, `.eps`) the
+        mixer's input is pre_norm(hidden_states + residual) -- hidden_states
+        alone without a residual -- computed in the in_proj's input pass; the
+        sum is written back into `residual`, as vLLM's fused add-RMSNorm does."""
+        return self._forward_impl(hidden_states, token_ids, pre_norm=pre_norm, residual=residual)
+
+    def forward_async(self, hidden_states, token_ids=None, *, pre_norm=None,
+                      residual=None) -> PendingReduce:
         """forward() with the channel-sharded all-reduce left in flight: returns a
         PendingReduce whose wait() yields the output.  Lets a caller overlap one
         step's (or chunk's) all-reduce with the next one's kernels; with
         tp_size == 1 the result is complete already."""
-        return self._forward_impl(hidden_states, token_ids, async_reduce=True)
+        return self._forward_impl(hidden_states, token_ids, async_reduce=True, pre_norm=pre_norm,
+                                  residual=residual)
 
     @staticmethod
     def _unpad(out, hidden_states, n_actual):
@@ -373,9 +398,9 @@ class HyenaMixerBase(nn.Module):
         full[:n_actual] = out
         return full
 
-    def _profile_run(self, hidden_states, token_ids=None):
+    def _profile_run(self, hidden_states, token_ids=None, pre_norm=None, residual=None):
         """attn_metadata is None during a memory-profiling pass (mixers.py:1230-1235)."""
-        z = self._project(hidden_states, token_ids)
+        z = self._project(hidden_states, token_ids, pre_norm, residual)
         y = z[:, 0::3] * z[:, 1::3] * z[:, 2::3]
         return self._out_proj(y.contiguous())
 

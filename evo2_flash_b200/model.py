@@ -101,10 +101,28 @@ class Evo2RMSNorm(nn.Module):
         self.hidden = hidden
 
     def forward(self, x, residual=None):
+        """norm(x), or (norm(x + residual), x + residual) (model.py:47-76).  On
+        CUDA one kernel pass (ops.rms_norm); the torch code is the CPU arm."""
+        if x.is_cuda:
+            from . import ops
+
+            s = torch.empty_like(x) if residual is not None else None
+            y, _ = ops.rms_norm(x, self.weight, self.eps, residual, s_out=s)
+            return y if residual is None else (y, s)
         if residual is not None:
             x = x + residual
             return self._norm(x), x
         return self._norm(x)
+
+    def add_norm_(self, x, residual):
+        """norm(x + residual), with residual <- x + residual in place (vLLM's
+        fused add-RMSNorm)."""
+        if x.is_cuda:
+            from . import ops
+
+            return ops.rms_norm(x, self.weight, self.eps, residual, s_out=residual)[0]
+        residual.add_(x)
+        return self._norm(residual)
 
     def _norm(self, x):
         y = x / (x.norm(2, dim=-1, keepdim=True) * self.hidden ** -0.5 + self.eps)
@@ -205,11 +223,21 @@ class Evo2DecoderLayer(nn.Module):
             self.mixer = mixer_factory(cfg, i, self.kind, k, f"layers.{i}.mixer", device)
         self.mlp = Evo2MLP(h, cfg.intermediate_size, use_act=(i == 0), device=device)
 
-    def forward(self, x, positions, segments):
-        pre = self.pre_norm(x)
-        m = self.mixer(pre, positions, segments) if self.kind == "attn" else self.mixer(pre)
-        post, x = self.post_norm(m, x)
-        return self.mlp(post) + x
+    def forward(self, x, positions, segments, add=None):
+        """One block (model.py:190-198) on the residual stream x, which it updates
+        in place.  `add`: the previous block's MLP output, not yet added to x
+        (None for the first block).  Returns (this block's MLP output, x): the
+        caller adds them in the next block's pre-norm or in the final norm, the
+        sum the reference forms at the end of each block."""
+        if self.kind != "attn" and getattr(self.mixer, "fuses_pre_norm", False):
+            # pre-norm, residual add and the in_proj quantisation in one pass
+            m = (self.mixer(x, pre_norm=self.pre_norm) if add is None
+                 else self.mixer(add, pre_norm=self.pre_norm, residual=x))
+        else:
+            pre = self.pre_norm(x) if add is None else self.pre_norm.add_norm_(add, x)
+            m = self.mixer(pre, positions, segments) if self.kind == "attn" else self.mixer(pre)
+        post = self.post_norm.add_norm_(m, x)  # x <- m + x
+        return self.mlp(post), x
 
 
 class StripedHyena2(nn.Module):
@@ -294,10 +322,11 @@ class StripedHyena2(nn.Module):
         `meta`: mixer metadata (prefill-only); `segments`: (row_start, row_end,
         seq_id, first_position) per sequence chunk in the step."""
         x = self.embed[input_ids]
+        add = None
         with set_forward_metadata(meta):
             for layer in self.layers:
-                x = layer(x, positions, segments)
-        return self.norm(x)
+                add, x = layer(x, positions, segments, add)
+        return self.norm.add_norm_(add, x)
 
     def logprobs(self, h, targets):
         logits = F.linear(h, self.embed).float()

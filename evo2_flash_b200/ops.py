@@ -246,6 +246,43 @@ def quant_e4m3(x, input_scale, out=None):
     return out
 
 
+def rms_norm(x, weight, eps, residual=None, *, want_y=True, quant_scale=None, s_out=None):
+    """Evo2RMSNorm of the decoder layer (model.py:47-76 Evo2RMSNorm.forward;
+    triton_norm.py:127-156 rms_norm), one pass over the rows of x (M, H) bf16:
+
+      s = x + residual (bf16), written to s_out (which may be x or residual:
+          vLLM's in-place fused add-norm);
+      y = weight * s / (||s||_2 * H^-0.5 + eps) with torch's bf16 roundings;
+      q = e4m3(clamp(y / quant_scale, +-448)) when quant_scale is given.
+
+    Returns (y or None, q or None).  want_y=False with quant_scale skips the
+    bf16 output entirely (the in_proj input of a Hyena layer)."""
+    _cuda(x, "x")
+    _require(x.dim() == 2 and x.dtype == BF16 and x.stride(1) == 1, "x must be (M, H) bf16 rows")
+    M, H = x.shape
+    _require(weight.dtype == BF16 and weight.numel() == H and weight.is_contiguous(),
+             "weight must be (H,) bf16")
+    if residual is not None:
+        _require(residual.shape == x.shape and residual.dtype == BF16 and residual.stride(1) == 1,
+                 "residual must match x")
+    if s_out is not None:
+        _require(s_out.shape == x.shape and s_out.dtype == BF16 and s_out.stride(1) == 1,
+                 "s_out must match x")
+    if quant_scale is not None:
+        _require(quant_scale.dtype == torch.float32 and quant_scale.numel() == 1,
+                 "quant_scale must be one fp32 element")
+    _require(want_y or quant_scale is not None or s_out is not None, "no output requested")
+    y = torch.empty(M, H, dtype=BF16, device=x.device) if want_y else None
+    q = torch.empty(M, H, dtype=E4M3, device=x.device) if quant_scale is not None else None
+    lib = _lib.load()
+    ld = lambda t: t.stride(0) if t is not None else 0  # noqa: E731
+    _lib.check(lib.hyena_rms_norm(
+        _ptr(x), x.stride(0), _ptr(residual), ld(residual), _ptr(weight), float(eps),
+        _ptr(s_out), ld(s_out), _ptr(y), ld(y), _ptr(q), ld(q), _ptr(quant_scale), M, H,
+        _stream()), "hyena_rms_norm")
+    return y, q
+
+
 def gemm_e4m3(a, b, scale_a, scale_b, out=None):
     """out (M, N) bf16 = (a (M,K) e4m3 . b (N,K) e4m3^T) * sa * sb (tcgen05)."""
     _require(a.dtype == E4M3 and b.dtype == E4M3, "e4m3 operands expected")

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define HYENA_ABI_VERSION 3
+#define HYENA_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define HYENA_API __attribute__((visibility("default")))
@@ -195,6 +195,26 @@ HYENA_API int hyena_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t
 /* Bytes of workspace the GEMMs above use at this shape: always 0 (kept so that
  * callers written against ABI version 2 keep working).  fp8 != 0 selects e4m3. */
 HYENA_API size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8);
+
+/* ---------------------------------------------------------------- decoder-layer norm
+ * Evo2RMSNorm (model.py:47-76; its CUDA form triton_norm.py:127-156 rms_norm)
+ * with the residual add and the in_proj input quantisation fused into one pass:
+ *   s = x + residual (bf16; residual NULL: s = x), stored to s_out if non-NULL
+ *       (s_out may alias x or residual: vLLM's in-place fused add-norm);
+ *   y = weight * bf16(s / bf16(bf16(bf16(||s||_2) * H^-0.5) + eps)), bf16,
+ *       stored to y if non-NULL;
+ *   q = e4m3(clamp(y / *input_scale, +-448)), stored to q if non-NULL (the rule
+ *       of hyena_quant_e4m3), so a Hyena layer's in_proj input never exists in
+ *       bf16.
+ * x, residual, s_out, y: (M, H) bf16 rows with strides that are multiples of 8
+ * elements, 16-byte aligned; q: (M, H) e4m3 rows of ldq (multiple of 8), 8-byte
+ * aligned; weight (H) bf16.  H % 8 == 0, H <= 16384; at least one output.  The
+ * fp32 sum of squares runs in this kernel's order, not ATen's: n may differ
+ * from the reference's in its last bf16 bit on rare rows. */
+HYENA_API int hyena_rms_norm(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                             const void* weight, float eps, void* s_out, int64_t lds, void* y,
+                             int64_t ldy, void* q, int64_t ldq, const float* input_scale,
+                             int32_t M, int32_t H, void* stream);
 
 /* ---------------------------------------------------------------- speculative bookkeeping
  * Position stamps: one fp32 per state block at stamps + block * stamp_stride

@@ -14,6 +14,7 @@ reference file:line it follows (paths relative to the evo2_flash project):
   LI segment .................... mixers.py:144-210 (+ gate order 1356-1397)
   decode / verify snapshots ..... mixers.py:555-663
   fp8 projection ................ fp8_emul.py:45-88
+  decoder-layer norm ............ model.py:47-76 (Evo2RMSNorm, + residual add)
   mixer forward ................. mixers.py:1277-1305 (FIR), 1327-1401 (LI)
 
 Pinning: `tests/golden/make_golden.py` runs the reference itself (its own CPU
@@ -264,6 +265,19 @@ def iir_snapshots(x, poles, res, state, tables):
         yt = (res[None] * st).sum(-1)
         out.index_add_(0, tok, yt.to(out.dtype) * active[:, None])
     return out
+
+
+# ---------------------------------------------------------------- decoder-layer norm
+def rms_norm(x, weight, eps, residual=None):
+    """Evo2RMSNorm (model.py:47-76): s = x (+ residual), y = weight * s /
+    (||s||_2 * H^-0.5 + eps), every op a bf16 torch op (eps outside the sqrt).
+    Returns y, or (y, s) with a residual, as the reference's forward does."""
+    if residual is not None:
+        s = x + residual
+        return rms_norm(s, weight, eps), s
+    h = x.shape[-1]
+    y = x / (x.norm(2, dim=-1, keepdim=True) * h ** -0.5 + eps)
+    return weight * y
 
 
 # ---------------------------------------------------------------- fp8 projection

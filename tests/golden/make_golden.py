@@ -17,7 +17,8 @@ Shims (the reference's mixers are vLLM modules; nothing here changes their math)
                                  after it (inner FIR / LI snapshots, gates, stamps)
                                  is the reference's own code.
   * EVO2_TORCH_SHORT_FIR=1    -> the reference's own torch twin for the K=3 prefill.
-The fp8 fixture calls the reference's fp8_emul functions directly.
+The fp8 fixture calls the reference's fp8_emul functions directly; the norm
+fixture runs the reference's Evo2RMSNorm (model.py) on CPU.
 
 Each fixture is a torch.save'd dict: config, parameters, and per step the
 metadata, the mixer input x, and the reference's in_proj output z, out_proj input
@@ -217,6 +218,37 @@ def fp8_fixture(ref_root):
     print("wrote fp8_in_proj.pt")
 
 
+def norm_fixture(ref_root):
+    """Evo2RMSNorm with and without the residual add, then the in_proj input
+    quantisation of its output.  Rows 0-15 hold multiples of 1/4 in [-4, 4]:
+    their sum of squares is exact in fp32 in any order, so a kernel that sums in
+    another order must still match them bit for bit; the other rows mix
+    magnitudes up to the 1e12 a late residual stream reaches."""
+    from evo2_flash import fp8_emul as FE
+    from evo2_flash.model import Evo2RMSNorm
+
+    g = torch.Generator().manual_seed(91)
+    rows, h = 48, 256
+    x = torch.randn(rows, h, generator=g)
+    x[:16] = torch.randint(-16, 17, (16, h), generator=g).float() / 4
+    x[32:] *= torch.logspace(0, 12, 16)[:, None]
+    x = x.to(BF)
+    r = torch.randn(rows, h, generator=g)
+    r[:16] = torch.randint(-4, 5, (16, h), generator=g).float() / 4  # sums stay on the grid
+    r = r.to(BF)
+    norm = Evo2RMSNorm(h, 1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(1 + 0.1 * torch.randn(h, generator=g))
+        norm.weight.data = norm.weight.data.to(BF)
+        y = norm(x)
+        y_add, s_add = norm(x, r)
+    sx = torch.tensor(4.0 / 448.0)
+    torch.save({"x": x, "r": r, "weight": norm.weight.data.clone(), "eps": 1e-6, "y": y,
+                "y_add": y_add, "s_add": s_add, "sx": sx,
+                "q_add": FE.quantize_input(y_add, sx)}, HERE / "rms_norm.pt")
+    print("wrote rms_norm.pt")
+
+
 def main(ref_root):
     M = _import_reference(ref_root)
     torch.manual_seed(0)
@@ -257,6 +289,7 @@ def main(ref_root):
             mm(slots, [1, 3], [], computed=[47, 53], num_spec=3),
         ], seed=5 + k)
     fp8_fixture(ref_root)
+    norm_fixture(ref_root)
 
 
 if __name__ == "__main__":

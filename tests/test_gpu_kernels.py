@@ -269,6 +269,120 @@ def test_quant_e4m3_exact():
     assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(ref))
 
 
+def _all_finite_bf16(cols=512):
+    """Every finite bf16 value once, as (rows, cols) rows (zero padded)."""
+    x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    x = x[torch.isfinite(x)]
+    pad = (-x.numel()) % cols
+    return torch.cat([x, torch.zeros(pad, dtype=torch.bfloat16)]).view(-1, cols)
+
+
+@pytest.mark.parametrize("sx", [0.01, 4.0 / 448.0, 1.0 / 3.0, 0.1, 2.0 ** -5, 3.3e-3, 1e-39,
+                                7.5e30])
+def test_quant_e4m3_every_bf16_value(sx):
+    """The quantiser divides by a reciprocal multiply and falls back to the
+    correctly rounded division near rounding ties: every finite bf16 value must
+    give the byte of the oracle's division (1e-39 is an fp32 subnormal scale,
+    which takes the division everywhere)."""
+    from evo2_flash_b200 import ops
+
+    x = _all_finite_bf16()
+    s = torch.tensor([sx], dtype=torch.float32)
+    ref = O.quantize_input(x, s).to(torch.float8_e4m3fn).view(torch.uint8)
+    q = ops.quant_e4m3(x.to(DEV), s.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(q.view(torch.uint8).cpu(), ref)
+
+
+def _grid_rows(rows, h, seed, lim=16):
+    """Multiples of 1/4 in [-lim/4, lim/4]: a row's sum of squares is exact in fp32
+    in any order (up to h = 16384), so the kernel's n equals the oracle's."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randint(-lim, lim + 1, (rows, h), generator=g).float() / 4).to(torch.bfloat16)
+
+
+def test_rms_norm_matches_reference_fixture():
+    from evo2_flash_b200 import ops
+    from tests.helpers import load_fixture
+
+    fx = load_fixture("rms_norm")
+    x, r, w = fx["x"].to(DEV), fx["r"].to(DEV), fx["weight"].to(DEV)
+    sx = fx["sx"].reshape(1).float().to(DEV)
+    y, _ = ops.rms_norm(x, w, fx["eps"])
+    s = torch.empty_like(x)
+    y2, q2 = ops.rms_norm(x, w, fx["eps"], r, quant_scale=sx, s_out=s)
+    torch.cuda.synchronize()
+    y, y2, s, q2 = y.cpu(), y2.cpu(), s.cpu(), q2.float().cpu()
+    assert torch.equal(s, fx["s_add"])
+    # rows 0-15: sums of squares exact in any order -> bit for bit
+    assert torch.equal(y[:16], fx["y"][:16]) and torch.equal(y2[:16], fx["y_add"][:16])
+    assert torch.equal(q2[:16], fx["q_add"][:16])
+    # other rows: n may differ in its last bf16 bit from the reference's order
+    for got, ref in ((y, fx["y"]), (y2, fx["y_add"])):
+        assert max_rel_err(got, ref) < 1e-2
+        assert (got == ref).float().mean() > 0.99
+    same = (y2 == fx["y_add"]).all(dim=1)
+    assert torch.equal(q2[same], fx["q_add"][same])
+
+
+@pytest.mark.parametrize("h", [4096, 8192, 1000, 12288])
+def test_rms_norm_exact_rows_with_residual_and_quant(h):
+    from evo2_flash_b200 import ops
+
+    x = _grid_rows(700, h, seed=h)
+    r = _grid_rows(700, h, seed=h + 1, lim=4)
+    g = torch.Generator().manual_seed(5)
+    w = (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)
+    sx = torch.tensor([6.0 / 448.0])
+    ref_y = O.rms_norm(x, w, 1e-6)
+    ref_y2, ref_s = O.rms_norm(x, w, 1e-6, r)
+    ref_q = O.quantize_input(ref_y2, sx)
+    xd, rd, wd = x.to(DEV), r.to(DEV), w.to(DEV)
+    y, none = ops.rms_norm(xd, wd, 1e-6)
+    assert none is None
+    # in place into the residual (vLLM's fused add-norm), y not materialised
+    none, q = ops.rms_norm(xd, wd, 1e-6, rd, want_y=False, quant_scale=sx.to(DEV), s_out=rd)
+    assert none is None
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), ref_y)
+    assert torch.equal(rd.cpu(), ref_s)
+    assert torch.equal(q.float().cpu(), ref_q)
+    # in place into x, bf16 output this time
+    xd2 = x.to(DEV)
+    y3, _ = ops.rms_norm(xd2, wd, 1e-6, r.to(DEV), s_out=xd2)
+    torch.cuda.synchronize()
+    assert torch.equal(xd2.cpu(), ref_s) and torch.equal(y3.cpu(), ref_y2)
+
+
+def test_rms_norm_random_rows_within_tolerance():
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn(3000, 4096, generator=g) * torch.logspace(-3, 9, 3000)[:, None]).to(
+        torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16)
+    ref = O.rms_norm(x, w, 1e-6)
+    y, _ = ops.rms_norm(x.to(DEV), w.to(DEV), 1e-6)
+    torch.cuda.synchronize()
+    y = y.cpu()
+    assert max_rel_err(y, ref) < 1e-2
+    assert (y == ref).float().mean() > 0.99
+
+
+def test_rms_norm_rejects_bad_arguments():
+    from evo2_flash_b200 import ops
+
+    x = torch.zeros(4, 4096, dtype=torch.bfloat16, device=DEV)
+    w = torch.ones(4096, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        ops.rms_norm(x, w[:100], 1e-6)
+    with pytest.raises(ValueError):
+        ops.rms_norm(x, w, 1e-6, want_y=False)
+    with pytest.raises(ValueError):  # H above the kernel's 16384
+        ops.rms_norm(torch.zeros(2, 16392, dtype=torch.bfloat16, device=DEV),
+                     torch.ones(16392, dtype=torch.bfloat16, device=DEV), 1e-6)
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
                                    (4096, 12288, 4096), (128, 12288, 4096), (1024, 4096, 4096),
                                    (7, 4096, 256)])

@@ -71,3 +71,37 @@ def test_profile_run_without_metadata():
     y = zb[:, 0::3] * zb[:, 1::3] * zb[:, 2::3]
     ref = y.float() @ m.out_proj.weight.float().t() + m.out_proj.bias.float()
     assert max_rel_err(out, ref) < REL_TOL
+
+
+@pytest.mark.parametrize("name", ["hcm_prefill", "hcl_mixed"])
+@pytest.mark.parametrize("fp8", [True, False])
+def test_pre_norm_fused_into_the_in_proj_pass(name, fp8):
+    """forward(add, pre_norm=norm, residual=x) == forward(norm(add + x)), with x
+    updated to add + x in place, for the fp8 and the bf16 projection."""
+    from evo2_flash_b200 import set_forward_metadata
+    from evo2_flash_b200.model import Evo2RMSNorm
+
+    fx = load_fixture(name)
+    H = fx["H"]
+    g = torch.Generator().manual_seed(3)
+    norm = Evo2RMSNorm(H, 1e-6, DEV)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16))
+    step = fx["steps"][0]
+    add = step["x"].to(DEV)
+    x0 = (torch.randn(add.shape, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    outs = []
+    for fused in (True, False):
+        m = build_mixer(fx, fp8=fp8)
+        x = x0.clone()
+        with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+            if fused:
+                out = m(add, pre_norm=norm, residual=x)
+            else:
+                pre, x = norm(add, x)
+                out = m(pre)
+        torch.cuda.synchronize()
+        outs.append((out.cpu(), x.cpu()))
+    assert torch.equal(outs[0][1], (add.cpu().float() + x0.cpu().float()).to(torch.bfloat16))
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(outs[0][0], outs[1][0])

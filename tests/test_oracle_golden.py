@@ -57,6 +57,15 @@ def test_fp8_quantisation_and_hopper_model():
     assert max_rel_err(exact, fx["out_hopper"]) < 2e-2
 
 
+def test_rms_norm_matches_reference():
+    fx = load_fixture("rms_norm")
+    y = O.rms_norm(fx["x"], fx["weight"], fx["eps"])
+    assert torch.equal(y, fx["y"])
+    y_add, s_add = O.rms_norm(fx["x"], fx["weight"], fx["eps"], fx["r"])
+    assert torch.equal(s_add, fx["s_add"]) and torch.equal(y_add, fx["y_add"])
+    assert torch.equal(O.quantize_input(y_add, fx["sx"]), fx["q_add"])
+
+
 def test_scan_equals_fft_segment():
     g = torch.Generator().manual_seed(0)
     H, L = 8, 700
