@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "hyena_b200.h"
@@ -64,6 +65,33 @@ __device__ __forceinline__ void pdl_entry() {
   pdl_wait();
 }
 
+// SMs of the current device (148 on B200).
+inline int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    sms = (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+              ? n : 148;
+  }
+  return sms;
+}
+
+// cudaFuncSetAttribute(Kern, MaxDynamicSharedMemorySize, bytes) once per
+// device (a function attribute belongs to the device's context).
+constexpr int HB_MAX_DEVICES = 64;
+template <auto Kern>
+inline bool smem_attr(int bytes) {
+  static std::atomic<int> done[HB_MAX_DEVICES];  // bytes set per device (0: none)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= HB_MAX_DEVICES) return false;
+  if (done[dev].load(std::memory_order_relaxed) == bytes) return true;
+  if (cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done[dev].store(bytes, std::memory_order_relaxed);
+  return true;
+}
+
 // Process-wide switch for the programmatic-serialisation attribute (on by
 // default; hyena_set_launch_chaining).
 bool launch_chaining();
@@ -104,36 +132,52 @@ __device__ __forceinline__ float bf16r(float x) {
 }
 __device__ __forceinline__ float ldbf(const bf16* p) { return __bfloat162float(*p); }
 
+// ---------------------------------------------------------------- cp.async
+// 16-byte global -> shared copies (L2 only), grouped and waited on per group.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---------------------------------------------------------------- quotients
 // A divide by a per-row or per-tensor divisor b whose fp32 quotient is then
 // rounded to a narrow type (bf16 or e4m3), with the result of the correctly
-// rounded __fdiv_rn but mostly without its cost.  rb = __frcp_rn(b); for b in
-// [2^-125, 2^125] and |a / b| in [2^-100, 2^100], p = fl(a * rb) differs from
-// a / b by at most 2^-23 |a / b| (two roundings of relative error 2^-24 each),
-// so p lies within 3 ulps of fl(a / b) in its binade, within 6 fp32 encodings
-// across a binade edge.  Rounding to the narrow type is monotonic, so when the
-// encodings 8 below and 8 above p convert to the same value, fl(a / b) does
-// too; otherwise (p near a rounding tie, or out of range) the quotient is
-// recomputed with __fdiv_rn.  a = 0 gives an exact p = +-0.
+// rounded __fdiv_rn but mostly at the cost of a multiply.  rb = __frcp_rn(b);
+// for b in [2^-125, 2^125] and a normal fp32 product p = fl(a * rb), p differs
+// from a / b by at most 2^-23 |a / b| (two roundings of relative error 2^-24),
+// so it lies within 3 ulps of fl(a / b) in its binade, within 6 encodings
+// across a binade edge.  Rounding to the narrow type is monotonic and changes
+// value only at its ties, which are fp32 encodings with fixed low bits (bf16:
+// low 16 bits 0x8000; normal e4m3, |p| >= 2^-6: low 20 bits 0x80000); when no
+// tie lies within 8 encodings of p, fl(a / b) rounds to the same value as p.
+// Otherwise (p near a tie, subnormal, zero, or an e4m3 subnormal) the quotient
+// is recomputed with __fdiv_rn.  e4m3 saturates at 448, so p beyond the normal
+// range (even inf) needs no check.
 __device__ __forceinline__ bool quot_divisor_ok(float b) {
   const float m = fabsf(b);
   return m >= 0x1p-125f && m <= 0x1p125f;
 }
-__device__ __forceinline__ bool quot_in_range(float p) {
-  const float m = fabsf(p);
-  return m >= 0x1p-100f && m <= 0x1p100f;
+// No bf16 tie within 8 encodings of p, and p a normal number.
+__device__ __forceinline__ bool quot_bf16_clear(uint32_t u) {
+  return ((u + 0x8008u) & 0xFFFFu) > 16u && ((u & 0x7F800000u) - 0x00800000u) < 0x7F000000u;
+}
+// No e4m3 tie within 8 encodings of p, and |p| >= 2^-6 (e4m3 normal or beyond).
+__device__ __forceinline__ bool quot_e4m3_clear(uint32_t u) {
+  return ((u + 0x80008u) & 0xFFFFFu) > 16u && (u & 0x7FFFFFFFu) >= 0x3C800000u;
 }
 // a / b rounded to bf16 (returned as fp32).
 __device__ __forceinline__ float quot_bf16(float a, float b, float rb, bool fast) {
-  if (fast) {
-    const float p = a * rb;
-    if (a == 0.0f) return p;
-    if (quot_in_range(p)) {
-      const uint32_t u = __float_as_uint(p);
-      const float lo = bf16r(__uint_as_float(u - 8u)), hi = bf16r(__uint_as_float(u + 8u));
-      if (lo == hi) return lo;
-    }
-  }
+  const float p = a * rb;
+  if (fast && quot_bf16_clear(__float_as_uint(p))) return bf16r(p);
   return bf16r(__fdiv_rn(a, b));
 }
 // (a0, a1) / b as a saturating e4m3 pair: clamp to +-448 then round to nearest
@@ -144,18 +188,9 @@ __device__ __forceinline__ __nv_fp8x2_storage_t e4m3x2(float x0, float x1) {
 }
 __device__ __forceinline__ __nv_fp8x2_storage_t quot_e4m3x2(float a0, float a1, float b, float rb,
                                                              bool fast) {
-  if (fast) {
-    const float p0 = a0 * rb, p1 = a1 * rb;
-    const bool z0 = a0 == 0.0f, z1 = a1 == 0.0f;
-    if ((z0 || quot_in_range(p0)) && (z1 || quot_in_range(p1))) {
-      const uint32_t u0 = __float_as_uint(p0), u1 = __float_as_uint(p1);
-      const __nv_fp8x2_storage_t lo = e4m3x2(z0 ? p0 : __uint_as_float(u0 - 8u),
-                                             z1 ? p1 : __uint_as_float(u1 - 8u));
-      const __nv_fp8x2_storage_t hi = e4m3x2(z0 ? p0 : __uint_as_float(u0 + 8u),
-                                             z1 ? p1 : __uint_as_float(u1 + 8u));
-      if (lo == hi) return lo;
-    }
-  }
+  const float p0 = a0 * rb, p1 = a1 * rb;
+  if (fast && quot_e4m3_clear(__float_as_uint(p0)) && quot_e4m3_clear(__float_as_uint(p1)))
+    return e4m3x2(p0, p1);
   return e4m3x2(__fdiv_rn(a0, b), __fdiv_rn(a1, b));
 }
 

@@ -424,6 +424,15 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
                ::: "memory");
 }
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -453,9 +462,6 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src,
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void epilogue_bar() {  // the four epilogue warps only
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-}
 template <int N>
 __host__ __device__ constexpr uint32_t pow2_cols() {
   return N <= 32 ? 32u : N <= 64 ? 64u : N <= 128 ? 128u : N <= 256 ? 256u : 512u;
@@ -464,12 +470,15 @@ __host__ __device__ constexpr uint32_t pow2_cols() {
 // One 128 x BN output tile per cluster of `splits` CTAs (grid (splits, tiles),
 // cluster (splits, 1, 1); splits = 1 is a plain one-tile-per-CTA GEMM).  CTA r
 // accumulates K blocks [r kblocks / splits, (r+1) kblocks / splits) in TMEM and
-// owns rows [r R, (r+1) R) of the tile.  After a cluster barrier (every ring is
-// idle) each CTA stages the rows other CTAs own in its shared memory and sends
-// each owner its rows with one bulk copy; every owner waits for its inbox on an
-// mbarrier, sums all ranks' partials in rank order (its own straight from TMEM;
-// deterministic), scales / adds bias and stores bf16.  A last cluster barrier
-// keeps every staging area alive until all copies have landed.
+// owns rows [r R, (r+1) R) of the tile.  Each CTA stages its whole fp32
+// partial tile in its own (idle) ring; once every CTA of the cluster has
+// finished its main loop (split arrive / wait cluster barrier, the staging in
+// between), each epilogue warp sends its rows to their owners with one bulk
+// copy per owner; every owner waits for its inbox on an mbarrier and all six
+// warps sum the ranks' partials in rank order (deterministic), scale / add
+// bias and store bf16 rows coalesced.  A second split barrier (arrive once the
+// inbox is full, wait before exit) keeps every staging area alive until all
+// copies have landed.
 template <bool FP8, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -574,31 +583,33 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
   }
   bool have = false;
   float scale = 1.0f, scale_b = 1.0f;
+  if constexpr (FP8) {  // every warp takes part in the final reduction
+    scale = __ldg(sa);
+    scale_b = __ldg(sb);
+  }
   if (warp >= 2) {
     // While the main loop runs: epilogue constants into registers / shared memory.
-    if constexpr (FP8) {
-      scale = __ldg(sa);
-      scale_b = __ldg(sb);
-    } else {
+    if constexpr (!FP8) {
       for (int j = threadIdx.x - 64; j < BN; j += 128)
         S.bias_s[j] = (bias != nullptr && n0 + j < N) ? __bfloat162float(bias[n0 + j]) : 0.0f;
     }
     have = __all_sync(0xffffffffu, kb1 > kb0 && mbar_wait(&S.acc_full, 0));
   }
-  // Barrier 1: in every CTA of the cluster the main loop is over (producer
-  // drained, accumulator complete), so every ring may now be staging / inbox.
+  // Barrier 1 (split arrive / wait): once every CTA of the cluster has arrived
+  // its main loop is over (producer drained, accumulator complete), so every
+  // ring may be staging / inbox.  Each CTA stages into its own ring between
+  // its arrive and its wait.
   fence_before();
   __syncwarp();
-  cluster_sync_all();
-  fence_after();
+  cluster_arrive();
 
-  const int q = warp & 3;  // TMEM lane quarter of an epilogue warp
-  const int row = 32 * q + lane;
-  const int owner = row / rows_per;
   if (warp >= 2) {
-    // Stage the rows other ranks own (an empty K slice stages zeros).
-    const bool stage = owner != rank && row < rows;
-    if (__any_sync(0xffffffffu, stage)) {
+    const int q = warp & 3;  // TMEM lane quarter of this epilogue warp
+    const int row = 32 * q + lane;
+    // Stage every row of the partial tile as fp32 (an empty K slice stages
+    // zeros): the rows other ranks own go out by bulk copy, this rank's own
+    // rows are summed from here with the inbox.
+    if (__any_sync(0xffffffffu, row < rows)) {  // warp-uniform: TMEM loads are .sync.aligned
       float4* dst = reinterpret_cast<float4*>(staging + row * LD);
 #pragma unroll 1
       for (int cb = 0; cb < BN / 32; cb += 2) {
@@ -611,7 +622,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[0][j] = r[1][j] = 0u;
         }
-        if (stage) {
+        if (row < rows) {
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -622,107 +633,89 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
         }
       }
     }
-    fence_proxy_async_smem();  // staged rows -> visible to the bulk-copy engine
-    epilogue_bar();
-    if (threadIdx.x == 64) {
-      for (int o = 0; o < splits; ++o) {
-        const int n = owned(o);
-        if (o == rank || n == 0) continue;
+    fence_proxy_async_smem();  // this warp's staged rows -> visible to the bulk-copy engine
+    __syncwarp();
+    cluster_wait();  // barrier 1: every peer's ring is free for its inbox
+    fence_after();
+    // This warp's rows to their owners: one bulk copy per row, issued by the
+    // row's lane, so that 32 copies per warp are in flight at once.
+    {
+      const int o = row / rows_per;
+      if (row < rows && o != rank) {
         const int slot = rank < o ? rank : rank - 1;
         const uint32_t dst =
-            map_to_rank(su32(inbox + slot * rows_per * LD), (uint32_t)o);
+            map_to_rank(su32(inbox + (slot * rows_per + row - o * rows_per) * LD), (uint32_t)o);
         const uint32_t bar = map_to_rank(su32(&S.inbox_full), (uint32_t)o);
-        bulk_copy_to_cluster(dst, su32(staging + o * rows_per * LD), uint32_t(n * LD * 4), bar);
+        bulk_copy_to_cluster(dst, su32(staging + row * LD), uint32_t(LD * 4), bar);
       }
     }
-    // Reduce own rows: all ranks' partials in rank order, this rank's from TMEM.
-    const bool mine = owner == rank && row < rows;
-    if (__any_sync(0xffffffffu, mine)) {
-      const bool ready = inbox_bytes == 0 || mbar_wait(&S.inbox_full, 0);
-      const int lr = row - rank * rows_per;
-      // This row's own scratch for its bf16 result (inbox slot 0, read up to
-      // the column written; the staging row when nothing is inboxed), stored
-      // coalesced below.
-      uint4* rowbuf = reinterpret_cast<uint4*>(splits > 1 ? inbox + lr * LD : staging + row * LD);
+  } else {
+    __syncwarp();
+    cluster_wait();  // barrier 1
+  }
+  // Barrier 2 arrive: every copy into this CTA has landed (the wait at the end
+  // keeps each CTA alive until its own outgoing copies have landed too).
+  const bool ready = inbox_bytes == 0 || mbar_wait(&S.inbox_full, 0);
+  __syncwarp();
+  cluster_arrive_relaxed();  // orders nothing: the inbox mbarrier already did
+  // Owned rows, by all warps, 4 columns per item and U items in flight per
+  // thread: the ranks' partials summed in rank order (deterministic), scaled /
+  // bias added, 4 bf16 stored (consecutive threads: consecutive 16-byte float4
+  // reads, conflict-free, and consecutive 8-byte pieces of a row).
+  if (__syncthreads_and(ready ? 1 : 0)) {
+    constexpr int CPR = BN / 4;  // 4-column pieces per row
+    constexpr int U = 8;
+    const int n_items = my_rows * CPR;
+    const int base = rank * rows_per;
 #pragma unroll 1
-      for (int cb = 0; cb < BN / 32; cb += 2) {
-        uint32_t r[2][32];
-        if (have) {
-          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32), r[0]);
-          tmem_ld32_async(tmem + (uint32_t(32 * q) << 16) + uint32_t(cb * 32 + 32), r[1]);
-          tmem_wait_ld();
-        } else {
+    for (int i0 = (int)threadIdx.x; i0 < n_items; i0 += U * THREADS) {
+      float4 acc[U];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[0][j] = r[1][j] = 0u;
-        }
-        if (!mine || !ready) continue;
+      for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < splits; ++p) {
+        const float* pb = p == rank ? staging + base * LD
+                                    : inbox + (p < rank ? p : p - 1) * rows_per * LD;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c0 = (cb + h) * 32;
-          float acc[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-          for (int p = 0; p < splits; ++p) {
-            if (p == rank) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(r[h][j]);
-            } else {
-              const int slot = p < rank ? p : p - 1;
-              const float4* src =
-                  reinterpret_cast<const float4*>(inbox + (slot * rows_per + lr) * LD + c0);
-#pragma unroll
-              for (int v = 0; v < 8; ++v) {
-                const float4 x = src[v];
-                acc[4 * v] += x.x;
-                acc[4 * v + 1] += x.y;
-                acc[4 * v + 2] += x.z;
-                acc[4 * v + 3] += x.w;
-              }
-            }
-          }
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 pk;
-            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float x0 = acc[8 * v + 2 * e], x1 = acc[8 * v + 2 * e + 1];
-              if constexpr (FP8) {
-                x0 = (x0 * scale) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
-                x1 = (x1 * scale) * scale_b;
-              } else {
-                x0 += S.bias_s[c0 + 8 * v + 2 * e];
-                x1 += S.bias_s[c0 + 8 * v + 2 * e + 1];
-              }
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
-              pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
-            rowbuf[(cb + h) * 4 + v] = pk;
+        for (int u = 0; u < U; ++u) {
+          const int it = i0 + u * THREADS;
+          if (it < n_items) {
+            const float4 x =
+                *reinterpret_cast<const float4*>(pb + (it / CPR) * LD + (it % CPR) * 4);
+            acc[u].x += x.x;
+            acc[u].y += x.y;
+            acc[u].z += x.z;
+            acc[u].w += x.w;
           }
         }
       }
-    }
-    // Coalesced store of the owned rows: one row per warp step, 16 bytes a lane.
-    epilogue_bar();
-    {
-      constexpr int VPR = BN / 8;  // 16-byte vectors per row
-      const int ew = warp - 2;
-      for (int lr = ew; lr < my_rows; lr += 4) {
-        const int rrow = rank * rows_per + lr;
-        const uint4* rowbuf = reinterpret_cast<const uint4*>(
-            splits > 1 ? inbox + lr * LD : staging + rrow * LD);
-        bf16* dst = out + (long long)(m0 + rrow) * ldo + n0;
-        for (int v = lane; v < VPR; v += 32) {
-          if (n0 + 8 * v < N) *reinterpret_cast<uint4*>(dst + 8 * v) = rowbuf[v];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int it = i0 + u * THREADS;
+        if (it >= n_items) continue;
+        const int lr = it / CPR, c = (it % CPR) * 4;
+        float v[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (FP8) {
+            v[e] = (v[e] * scale) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+          } else {
+            v[e] += S.bias_s[c + e];
+          }
+        }
+        if (n0 + c < N) {
+          const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+          const __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+          uint2 pk;
+          pk.x = *reinterpret_cast<const uint32_t*>(&h0);
+          pk.y = *reinterpret_cast<const uint32_t*>(&h1);
+          *reinterpret_cast<uint2*>(out + (long long)(m0 + base + lr) * ldo + n0 + c) = pk;
         }
       }
     }
   }
-  // Barrier 2: every bulk copy has landed (each owner waited for its inbox),
-  // so no staging area is still being read when its CTA exits.
-  fence_before();
-  __syncwarp();
-  cluster_sync_all();
+  // Barrier 2 wait: every owner has its inbox, so no staging area is still
+  // being read when its CTA exits; every TMEM read above is done.
+  cluster_wait();
   if (warp == 1) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -768,17 +761,6 @@ static int make_map(CUtensorMap* m, const void* base, bool fp8, uint64_t inner, 
 // stream.  Set through hyena_set_gemm_max_ctas.
 static std::atomic<int> g_max_ctas{0};
 
-static int num_sms() {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-      sms = 148;
-  }
-  return sms;
-}
-
 template <bool FP8, int BN>
 static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* out, int64_t ldo,
                      int M, int N, int K, const float* sa, const float* sb, const void* bias,
@@ -787,13 +769,7 @@ static int launch_bn(const CUtensorMap& ta, const void* B, int64_t ldb, void* ou
   int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
   if (rc) return rc;
   const size_t smem = sizeof(Smem<BN>) + 1024;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemm_kernel<FP8, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(gemm)");
-    attr = true;
-  }
+  if (!smem_attr<gemm_kernel<FP8, BN>>((int)smem)) return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
   const long long tiles = (long long)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
   long long cap = num_sms();
   const int lim = g_max_ctas.load(std::memory_order_relaxed);
@@ -811,12 +787,7 @@ static size_t cluster_smem() {
 
 template <bool FP8, int BN>
 static bool cluster_attr() {
-  static int state = 0;  // 0 unset, 1 ok, -1 failed
-  if (state == 0)
-    state = cudaFuncSetAttribute(gemm_cluster_kernel<FP8, BN>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)cluster_smem<FP8, BN>()) == cudaSuccess ? 1 : -1;
-  return state > 0;
+  return smem_attr<gemm_cluster_kernel<FP8, BN>>((int)cluster_smem<FP8, BN>());
 }
 
 // How many clusters of `splits` CTAs can be resident at once (0 if unknown).
@@ -855,7 +826,7 @@ static int launch_cluster(const CUtensorMap& ta, const void* B, int64_t ldb, voi
   CUtensorMap tb;
   int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN);
   if (rc) return rc;
-  if (!cluster_attr<FP8, BN>()) return check_launch("cudaFuncSetAttribute(gemm_cluster)");
+  if (!cluster_attr<FP8, BN>()) return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(gemm_cluster) failed");
   const int tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM);
   launch_kernel(gemm_cluster_kernel<FP8, BN>, dim3((unsigned)splits, (unsigned)tiles, 1),
                 dim3(THREADS), cluster_smem<FP8, BN>(), st, (unsigned)splits, ta, tb,

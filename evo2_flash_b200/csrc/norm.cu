@@ -35,22 +35,26 @@ __global__ void __launch_bounds__(NORM_THREADS) rms_norm_kernel(const NormArgs A
   const bool qfast = quot_divisor_ok(sx);
   const float rsx = __frcp_rn(sx);
   int parity = 0;
-  for (int row = blockIdx.x; row < A.M; row += gridDim.x, parity ^= 1) {
-    uint4 xv[NV];
+  // x (and r) of a row, loaded by this thread; the next row's are issued
+  // before the current row is reduced, so two rows per CTA are in flight.
+  uint4 xv[NV], rv[NV], xn[NV], rn_[NV];
+  auto load_row = [&](int row, uint4 (&xa)[NV], uint4 (&ra)[NV]) {
     const uint4* xr = reinterpret_cast<const uint4*>(A.x + (long long)row * A.ldx);
+    const uint4* rr =
+        A.r != nullptr ? reinterpret_cast<const uint4*>(A.r + (long long)row * A.ldr) : nullptr;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int v = tid + i * NORM_THREADS;
-      if (v < vpr) xv[i] = __ldcs(xr + v);
-    }
-    if (A.r != nullptr) {
-      const uint4* rr = reinterpret_cast<const uint4*>(A.r + (long long)row * A.ldr);
-      uint4 rv[NV];
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int v = tid + i * NORM_THREADS;
-        if (v < vpr) rv[i] = __ldcs(rr + v);
+      if (v < vpr) {
+        xa[i] = __ldcs(xr + v);
+        if (A.r != nullptr) ra[i] = __ldcs(rr + v);
       }
+    }
+  };
+  if ((int)blockIdx.x < A.M) load_row((int)blockIdx.x, xv, rv);
+  for (int row = blockIdx.x; row < A.M; row += gridDim.x, parity ^= 1) {
+    if (row + (int)gridDim.x < A.M) load_row(row + (int)gridDim.x, xn, rn_);
+    if (A.r != nullptr) {
       // bf16 + bf16 -> bf16: the exact sum rounded once (see packed math)
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
@@ -116,7 +120,28 @@ __global__ void __launch_bounds__(NORM_THREADS) rms_norm_kernel(const NormArgs A
             *reinterpret_cast<const uint2*>(o);
       }
     }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      xv[i] = xn[i];
+      rv[i] = rn_[i];
+    }
   }
+}
+
+// One resident wave: blocks = SMs x the blocks of this variant an SM holds.
+template <int NV>
+static int launch_norm(const NormArgs& A, cudaStream_t st) {
+  static const int per_sm = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, rms_norm_kernel<NV>, NORM_THREADS, 0) !=
+            cudaSuccess || n < 1)
+      n = 4;
+    return n;
+  }();
+  const int wave = num_sms() * per_sm;
+  launch_kernel(rms_norm_kernel<NV>, dim3(A.M < wave ? A.M : wave), dim3(NORM_THREADS), 0, st, 0u,
+                A);
+  return check_launch("rms_norm_kernel");
 }
 
 int rms_norm_launch(const NormArgs& A, cudaStream_t st) {
@@ -134,14 +159,11 @@ int rms_norm_launch(const NormArgs& A, cudaStream_t st) {
              "rms_norm: q misaligned");
   const int vpr = A.H / 8;
   const int nv = (vpr + NORM_THREADS - 1) / NORM_THREADS;
-  const int blocks = A.M < 148 * 8 ? A.M : 148 * 8;
-  const dim3 grid(blocks), block(NORM_THREADS);
-  if (nv <= 1) launch_kernel(rms_norm_kernel<1>, grid, block, 0, st, 0u, A);
-  else if (nv <= 2) launch_kernel(rms_norm_kernel<2>, grid, block, 0, st, 0u, A);
-  else if (nv <= 4) launch_kernel(rms_norm_kernel<4>, grid, block, 0, st, 0u, A);
-  else if (nv <= 8) launch_kernel(rms_norm_kernel<8>, grid, block, 0, st, 0u, A);
-  else launch_kernel(rms_norm_kernel<16>, grid, block, 0, st, 0u, A);
-  return check_launch("rms_norm_kernel");
+  if (nv <= 1) return launch_norm<1>(A, st);
+  if (nv <= 2) return launch_norm<2>(A, st);
+  if (nv <= 4) return launch_norm<4>(A, st);
+  if (nv <= 8) return launch_norm<8>(A, st);
+  return launch_norm<16>(A, st);
 }
 
 }  // namespace hb

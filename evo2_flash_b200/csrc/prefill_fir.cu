@@ -106,20 +106,6 @@ __device__ __forceinline__ void split_triples(uint32_t w0, uint32_t w1, uint32_t
   v = as_bf162(__byte_perm(w1, w2, 0x7610));
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Tiles walk the CTA's rows [r0, r1) and never straddle a segment boundary.
 struct TileIt {
   int r, n, j;
@@ -441,13 +427,8 @@ prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
 template <int K>
 static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, cudaStream_t st) {
   const size_t smem = sizeof(FirShared<K>);
-  static bool attr_set = false;  // per process; the attribute is per function
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(fir_prefill_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return check_launch("cudaFuncSetAttribute(fir_prefill)");
-    attr_set = true;
-  }
+  if (!smem_attr<fir_prefill_kernel<K>>((int)smem))
+    return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(fir_prefill) failed");
   // Rows per CTA: long enough that the (K-1)-row halo is a small fraction,
   // short enough to fill the 148 SMs several times over.
   const int groups = P.H / FIR_CG;

@@ -167,6 +167,7 @@ HYENA_API int hyena_decode(const hyena_layer_params* p, const hyena_decode_args*
  * the rule of fp8_emul.quantize_input (fp8_emul.py:76-78) and of vLLM's static
  * W8A8 path the reference in_proj uses (mixers.py:740-757, 780-783).
  * x: (M, K) bf16 with row stride ldx; q: (M, K) e4m3 contiguous rows of ldq.
+ * K % 8 == 0, K <= 16384.
  */
 HYENA_API int hyena_quant_e4m3(const void* x, int64_t ldx, void* q, int64_t ldq, int32_t M,
                      int32_t K, const float* input_scale, void* stream);
