@@ -25,6 +25,7 @@ namespace hb {
 constexpr int DEC_THREADS = 128;
 constexpr int DEC_MAXQ = 8;
 constexpr int DEC_MAXW0 = 8;
+constexpr int IIR_STAGE_MAXD = 20;  // widest S2 row (floats) the staged LI path handles
 
 template <int N>
 __device__ __forceinline__ float pick(const float (&v)[N], int i) {
@@ -188,24 +189,67 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     float s[16], pl[16], rs[16];
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
-      s[q] = src_ok ? st[src * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
-                         (long long)q * cs]
-                    : 0.0f;
       pl[q] = expf(P.log_poles[(long long)h * P.lp_stride_h + q * P.lp_stride_s]);
       rs[q] = P.residues[(long long)h * P.res_stride_h + q * P.res_stride_s];
     }
+    // Modes contiguous (S2 rows of D >= 16 floats, the stamp column included):
+    // a warp's 32 channels are one contiguous run of 32 D floats per block, so
+    // the state and every snapshot move through shared memory with coalesced
+    // 4-byte accesses (the stamp column is never written) instead of 16
+    // scattered ones per thread.
+    const long long D = A.inner_state.dim_stride;
+    const bool staged = cs == 1 && D >= 16 && D <= IIR_STAGE_MAXD;
+    if (staged) {
+      __shared__ float sm[DEC_THREADS / 32][32 * (IIR_STAGE_MAXD + 1)];
+      const int lane = threadIdx.x & 31;
+      float* w = sm[threadIdx.x >> 5];
+      const long long h0 = (long long)(h - lane);  // the warp's first channel
+      const int pitch = (int)(D | 1);  // odd row pitch: conflict-free row reads
+      const int run = 32 * (int)D;
+      const float* sp = st + src * A.inner_state.block_stride + h0 * D;
+      for (int j = lane; j < run; j += 32)
+        w[(j / (int)D) * pitch + j % (int)D] = src_ok ? sp[j] : 0.0f;
+      __syncwarp();
 #pragma unroll
-    for (int p = 0; p < DEC_MAXQ; ++p) {
-      if (p < n) {
+      for (int q = 0; q < 16; ++q) s[q] = w[lane * pitch + q];
 #pragma unroll
-        for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u[p]);
-        if (dok[p]) {
+      for (int p = 0; p < DEC_MAXQ; ++p) {
+        if (p < n) {  // n and dok[p] are per request: uniform in the warp
 #pragma unroll
-          for (int q = 0; q < 16; ++q)
-            st[dst[p] * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
-               (long long)q * cs] = s[q];
+          for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u[p]);
+          if (dok[p]) {
+            __syncwarp();  // the previous snapshot's stores have read the buffer
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[lane * pitch + q] = s[q];
+            __syncwarp();
+            float* dp = st + dst[p] * A.inner_state.block_stride + h0 * D;
+            for (int j = lane; j < run; j += 32) {
+              const int c = j % (int)D;
+              if (c < 16) dp[j] = w[(j / (int)D) * pitch + c];
+            }
+          }
+          y[p] = modal_readout16(s, rs);
         }
-        y[p] = modal_readout16(s, rs);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        s[q] = src_ok ? st[src * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
+                           (long long)q * cs]
+                      : 0.0f;
+#pragma unroll
+      for (int p = 0; p < DEC_MAXQ; ++p) {
+        if (p < n) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u[p]);
+          if (dok[p]) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              st[dst[p] * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride +
+                 (long long)q * cs] = s[q];
+          }
+          y[p] = modal_readout16(s, rs);
+        }
       }
     }
   }
