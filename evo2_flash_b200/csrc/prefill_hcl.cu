@@ -24,7 +24,7 @@ namespace hb {
 
 constexpr int HCL_C = 256;       // rows per chunk
 constexpr int HCL_CG = 128;      // channels per CTA (one thread per channel)
-constexpr int HCL_TILE = 32;     // rows staged in shared memory at a time
+constexpr int HCL_TILE = 16;     // rows staged in shared memory at a time
 constexpr int HCL_S = 16;        // modal order
 
 struct HclWorkspace {
@@ -89,8 +89,8 @@ __device__ __forceinline__ bool chunk_ctx(const hyena_prefill_args& A, const int
 }
 
 struct HclTile {
-  uint32_t zt[HCL_TILE][3 * HCL_CG / 2];  // z rows, raw bf16x2 words
-  uint32_t zh[2][3 * HCL_CG / 2];         // the two z rows before the tile
+  uint32_t zt[2][HCL_TILE][3 * HCL_CG / 2];  // z rows, raw bf16x2 words (double-buffered)
+  uint32_t zh[2][3 * HCL_CG / 2];            // the two z rows before the tile
   bf162 ug[HCL_TILE][HCL_CG / 2];         // u = bf16(x1*v), channel pairs
   bf162 x2g[HCL_TILE][HCL_CG / 2];
 };
@@ -151,20 +151,32 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
     S.zh[q][wd] = lo | (hi << 16);
   }
   const bf16* z = static_cast<const bf16*>(A.z);
+  constexpr int VPR = WORDS * 4 / 16;  // 16-byte vectors per z row of the CTA
+  // Tile k's z rows into buffer k & 1 with cp.async; one group per call.
+  auto issue = [&](int t0) {
+    if (t0 < c.row1) {
+      const int n = min(HCL_TILE, c.row1 - t0);
+      uint32_t(*dst)[WORDS] = S.zt[((t0 - c.row0) / HCL_TILE) & 1];
+      for (int i = tid; i < n * VPR; i += HCL_CG) {
+        const int row = i / VPR, v = i % VPR;
+        cp_async16(reinterpret_cast<uint4*>(&dst[row][0]) + v,
+                   reinterpret_cast<const uint4*>(z + (long long)(t0 + row) * A.ldz + 3 * c0) + v);
+      }
+    }
+    cp_async_commit();
+  };
+  issue(c.row0);
   for (int t0 = c.row0; t0 < c.row1; t0 += HCL_TILE) {
     const int n = min(HCL_TILE, c.row1 - t0);
-    constexpr int VPR = WORDS * 4 / 16;
-    for (int i = tid; i < n * VPR; i += HCL_CG) {
-      const int row = i / VPR, v = i % VPR;
-      *(reinterpret_cast<uint4*>(&S.zt[row][0]) + v) =
-          __ldg(reinterpret_cast<const uint4*>(z + (long long)(t0 + row) * A.ldz + 3 * c0) + v);
-    }
+    issue(t0 + HCL_TILE);  // the next tile loads while this one is processed
+    cp_async_wait<1>();
     __syncthreads();
+    const uint32_t(*zt)[WORDS] = S.zt[((t0 - c.row0) / HCL_TILE) & 1];
     {
       const int g0 = half * (HCL_TILE / 2);
       bf162 h2[3], h1[3];
-      const uint32_t* a = g0 >= 2 ? &S.zt[g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
-      const uint32_t* b = g0 >= 1 ? &S.zt[g0 - 1][3 * pp] : &S.zh[1][3 * pp];
+      const uint32_t* a = g0 >= 2 ? &zt[g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
+      const uint32_t* b = g0 >= 1 ? &zt[g0 - 1][3 * pp] : &S.zh[1][3 * pp];
       split_triples_hcl(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
       split_triples_hcl(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
 #pragma unroll 4
@@ -172,7 +184,7 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
         const int row = g0 + i;
         if (row < n) {
           bf162 cur[3], o[3];
-          split_triples_hcl(S.zt[row][3 * pp], S.zt[row][3 * pp + 1], S.zt[row][3 * pp + 2],
+          split_triples_hcl(zt[row][3 * pp], zt[row][3 * pp + 1], zt[row][3 * pp + 2],
                             cur[0], cur[1], cur[2]);
 #pragma unroll
           for (int col = 0; col < 3; ++col) {
@@ -187,8 +199,8 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
     }
     __syncthreads();
     for (int i = tid; i < WORDS; i += HCL_CG) {  // z history for the next tile
-      const uint32_t a0 = n >= 2 ? S.zt[n - 2][i] : S.zh[1][i];
-      const uint32_t a1 = S.zt[n - 1][i];
+      const uint32_t a0 = n >= 2 ? zt[n - 2][i] : S.zh[1][i];
+      const uint32_t a1 = zt[n - 1][i];
       S.zh[0][i] = a0;
       S.zh[1][i] = a1;
     }
@@ -198,6 +210,7 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
       fn(t0 + row, ldbf(xg + row * HCL_CG + tid), ldbf(ug + row * HCL_CG + tid));
     __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
 __device__ __forceinline__ void load_pole_pairs(const hyena_layer_params& P, int h, f2* p2) {
@@ -223,7 +236,8 @@ __device__ __forceinline__ float readout_pairs(const f2* s2, const f2* r2) {
 __global__ void __launch_bounds__(HCL_CG)
 hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
   pdl_entry();
-  __shared__ __align__(16) HclTile S;
+  extern __shared__ __align__(16) uint8_t hcl_smem[];
+  HclTile& S = *reinterpret_cast<HclTile*>(hcl_smem);
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
   if (c.k == c.nch - 1) return;  // the final chunk's aggregate is never needed
@@ -281,7 +295,8 @@ hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWork
 __global__ void __launch_bounds__(HCL_CG)
 hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWorkspace W) {
   pdl_entry();
-  __shared__ __align__(16) HclTile S;
+  extern __shared__ __align__(16) uint8_t hcl_smem[];
+  HclTile& S = *reinterpret_cast<HclTile*>(hcl_smem);
   ChunkCtx c;
   if (!chunk_ctx(A, W.chunk_base, blockIdx.x, c)) return;
   const int c0 = blockIdx.y * HCL_CG;
@@ -344,11 +359,16 @@ int hcl_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A,
   launch_kernel(hcl_plan_kernel, dim3(1), dim3(32), 0, st, 0u, A.query_start_loc, A.num_segments, W.chunk_base);
   int rc = check_launch("hcl_plan_kernel");
   if (rc) return rc;
-  launch_kernel(hcl_aggregate_kernel, dim3(max_chunks, groups), dim3(HCL_CG), 0, st, 0u, P, A, W);
+  const int smem = (int)sizeof(HclTile);
+  if (!smem_attr<hcl_aggregate_kernel>(smem) || !smem_attr<hcl_output_kernel>(smem))
+    return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(hcl) failed");
+  launch_kernel(hcl_aggregate_kernel, dim3(max_chunks, groups), dim3(HCL_CG), (size_t)smem, st, 0u,
+                P, A, W);
   if ((rc = check_launch("hcl_aggregate_kernel"))) return rc;
   launch_kernel(hcl_carry_kernel, dim3(A.num_segments, (P.H * HCL_S + 127) / 128), dim3(128), 0, st, 0u, P, A, W);
   if ((rc = check_launch("hcl_carry_kernel"))) return rc;
-  launch_kernel(hcl_output_kernel, dim3(max_chunks, groups), dim3(HCL_CG), 0, st, 0u, P, A, W);
+  launch_kernel(hcl_output_kernel, dim3(max_chunks, groups), dim3(HCL_CG), (size_t)smem, st, 0u,
+                P, A, W);
   if ((rc = check_launch("hcl_output_kernel"))) return rc;
   return conv_state_update_launch(P, A, st);
 }
