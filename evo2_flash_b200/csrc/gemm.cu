@@ -389,7 +389,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // with R = ceil(BM / splits) and rows padded to LD = BN + 4 floats, so that a
 // warp's 16-byte accesses to 32 consecutive rows fall in distinct banks.
 template <int BN>
-constexpr int max_cluster_splits() {
+__host__ __device__ constexpr int max_cluster_splits() {
   return BN >= 256 ? 3 : 4;
 }
 constexpr int max_inbox_rows(int ms) {  // max over splits 2..ms of (splits-1) ceil(BM/splits)
@@ -665,6 +665,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
   if (__syncthreads_and(ready ? 1 : 0)) {
     constexpr int CPR = BN / 4;  // 4-column pieces per row
     constexpr int U = 8;
+    constexpr int MAXS = max_cluster_splits<BN>();
     const int n_items = my_rows * CPR;
     const int base = rank * rows_per;
 #pragma unroll 1
@@ -672,7 +673,9 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
       float4 acc[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < splits; ++p) {
+#pragma unroll
+      for (int p = 0; p < MAXS; ++p) {  // unrolled: every partial's loads in flight together
+        if (p >= splits) break;
         const float* pb = p == rank ? staging + base * LD
                                     : inbox + (p < rank ? p : p - 1) * rows_per * LD;
 #pragma unroll
