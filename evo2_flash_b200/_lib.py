@@ -13,7 +13,7 @@ from ._build import LIB_PATH
 
 HYENA_KIND_FIR = 0
 HYENA_KIND_IIR = 1
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class StateView(C.Structure):
@@ -113,6 +113,9 @@ SIGNATURES = {
                                  C.c_float, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
                                  C.c_void_p, C.c_int64, C.c_void_p, C.c_int32, C.c_int32,
                                  C.c_void_p]),
+    "hyena_gemm_fp8_emulated": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                                          C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
+                                          C.c_void_p, C.c_void_p, C.c_void_p]),
     "hyena_gemm_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     "hyena_set_gemm_max_ctas": (None, [C.c_int32]),
     "hyena_set_launch_chaining": (None, [C.c_int32]),

@@ -39,6 +39,9 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
                      int64_t ldo, int M, int N, int K, const void* bias, void* ws,
                      size_t ws_bytes, cudaStream_t st);
 size_t gemm_workspace_size(int M, int N, int K, bool fp8);
+int gemm_fp8_emulated_launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                             int64_t ldo, int N, int M, int K, const float* sa, const float* sb,
+                             cudaStream_t st);
 void gemm_set_max_ctas(int n);
 int spec_accepted_launch(const int32_t* slots, int64_t slot_stride, int num_reqs,
                          const int32_t* computed, const float* stamps, int64_t stamp_stride,
@@ -186,6 +189,13 @@ int hyena_rms_norm(const void* x, int64_t ldx, const void* residual, int64_t ldr
                  // H ** -0.5 as a Python float, then the fp32 scalar torch multiplies by
                  static_cast<float>(std::pow(static_cast<double>(H), -0.5)), eps};
   return hb::rms_norm_launch(A, static_cast<cudaStream_t>(stream));
+}
+
+int hyena_gemm_fp8_emulated(const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
+                            int64_t ldo, int32_t N, int32_t M, int32_t K, const float* scale_a,
+                            const float* scale_b, void* stream) {
+  return hb::gemm_fp8_emulated_launch(A, lda, B, ldb, out, ldo, N, M, K, scale_a, scale_b,
+                                      static_cast<cudaStream_t>(stream));
 }
 
 size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8) {

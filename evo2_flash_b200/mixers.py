@@ -76,6 +76,28 @@ class Bf16Linear(nn.Module):
         return ops.gemm_bf16(x, self.weight, bias), None
 
 
+class ProjectionTap(nn.Module):
+    """Parameter-free stand-in for in_proj in FP8-surgery layers whose projection
+    is a token table or the fully emulated GEMM (mixers.py:681-688): forward(z)
+    -> (z, None), so a hook on in_proj still sees the projection output."""
+
+    def forward(self, z):
+        return z, None
+
+
+class HybridProjection(Bf16Linear):
+    """bf16 in_proj whose calibrated worst output channels are recomputed by the
+    emulated FP8 GEMM inside the module (mixers.py:691-702), so hooks see the
+    final projection.  `emulate(x) -> (cols, values)` is attached by the mixer."""
+
+    emulate = None
+
+    def forward(self, x):
+        z, _ = super().forward(x)
+        cols, emul = self.emulate(x)
+        return z.index_copy(-1, cols, emul), None
+
+
 # ---------------------------------------------------------------- helpers
 def _cache_safe_state_indices(indices, state):
     """vLLM's undersized profiling cache: use null block 0 (mixers.py:527-540)."""
@@ -164,7 +186,42 @@ class HyenaMixerBase(nn.Module):
             raise ValueError("the short filter kernels implement K_short = 3")
         self.num_spec = int(num_spec or 0)
         self.use_fp8 = bool(getattr(config, "use_fp8_input_projections", False))
-        if self.use_fp8:
+        # FP8-surgery layers (mixers.py:758-800): a per-token table, the fully
+        # emulated Hopper GEMM, or a bf16 projection with emulated channels.
+        self.in_proj_token_table = None
+        self.in_proj_emul_weight_t = None
+        self.in_proj_emul_scales = None
+        self.in_proj_emul_cols = None
+        chan = getattr(config, "hyena_fp8_emulated_channels", None) or {}
+        n_emul = int(chan.get(layer_idx, 0)) if isinstance(chan, dict) else 0
+        token_layers = tuple(getattr(config, "hyena_token_table_layers", None) or ())
+        emul_layers = tuple(getattr(config, "hyena_fp8_emulated_layers", None) or ())
+        surgery = layer_idx in token_layers or layer_idx in emul_layers or n_emul > 0
+        if surgery and tp_size != 1:
+            raise ValueError(f"{prefix}: FP8-surgery layers are not channel-sharded (tp_size must be 1)")
+        bf16 = dict(dtype=torch.bfloat16, device=device)
+        if layer_idx in token_layers:
+            self.in_proj = ProjectionTap()
+            self.in_proj_token_table = nn.Parameter(
+                torch.empty(config.vocab_size, 3 * h, **bf16), requires_grad=False)
+        elif layer_idx in emul_layers:
+            self.in_proj = ProjectionTap()
+            self.in_proj_emul_weight_t = nn.Parameter(torch.empty(h, 3 * h, **bf16),
+                                                      requires_grad=False)
+            self.in_proj_emul_scales = nn.Parameter(
+                torch.empty(2, dtype=torch.float32, device=device), requires_grad=False)
+        elif n_emul:
+            self.in_proj = HybridProjection(h, 3 * h, bias=False, device=device)
+            self.in_proj_emul_weight_t = nn.Parameter(torch.empty(h, n_emul, **bf16),
+                                                      requires_grad=False)
+            self.in_proj_emul_scales = nn.Parameter(
+                torch.empty(2, dtype=torch.float32, device=device), requires_grad=False)
+            self.in_proj_emul_cols = nn.Parameter(
+                torch.empty(n_emul, dtype=torch.int64, device=device), requires_grad=False)
+            self.in_proj.emulate = lambda x: (
+                self.in_proj_emul_cols,
+                ops.fp8_linear_emulated(x, self.in_proj_emul_weight_t, self.in_proj_emul_scales))
+        elif self.use_fp8:
             self.in_proj = Fp8InProj(h, 3 * hl, device=device)
         else:
             self.in_proj = Bf16Linear(h, 3 * hl, bias=False, device=device)
@@ -288,6 +345,26 @@ class HyenaMixerBase(nn.Module):
 
     # ---- forward ----------------------------------------------------------------
     def _project(self, hidden_states, token_ids=None, pre_norm=None, residual=None):
+        """in_proj, or for FP8-surgery layers the token table / the emulated GEMM,
+        always returned through self.in_proj (mixers.py:1076-1092)."""
+        if isinstance(self.in_proj, ProjectionTap):
+            if pre_norm is not None and self.in_proj_token_table is None:
+                hidden_states, _ = ops.rms_norm(hidden_states, pre_norm.weight, pre_norm.eps,
+                                                residual, s_out=residual)
+            elif pre_norm is not None and residual is not None:
+                # the table ignores the normed input; the residual add still happens
+                ops.rms_norm(hidden_states, pre_norm.weight, pre_norm.eps, residual, want_y=False,
+                             s_out=residual)
+            if self.in_proj_token_table is not None:
+                if token_ids is None:
+                    raise ValueError(
+                        f"{self.prefix}: token-table projection needs input_ids "
+                        "(inputs_embeds are unsupported for FP8-surgery checkpoints)")
+                z, _ = self.in_proj(self.in_proj_token_table[token_ids[: hidden_states.shape[0]]])
+                return z
+            z, _ = self.in_proj(ops.fp8_linear_emulated(hidden_states, self.in_proj_emul_weight_t,
+                                                        self.in_proj_emul_scales))
+            return z
         if pre_norm is not None:
             # The decoder layer's pre-norm (and residual add) in the in_proj's input
             # pass: with the fp8 projection and no hook on it, the normed input

@@ -223,7 +223,7 @@ class Evo2DecoderLayer(nn.Module):
             self.mixer = mixer_factory(cfg, i, self.kind, k, f"layers.{i}.mixer", device)
         self.mlp = Evo2MLP(h, cfg.intermediate_size, use_act=(i == 0), device=device)
 
-    def forward(self, x, positions, segments, add=None):
+    def forward(self, x, positions, segments, add=None, input_ids=None):
         """One block (model.py:190-198) on the residual stream x, which it updates
         in place.  `add`: the previous block's MLP output, not yet added to x
         (None for the first block).  Returns (this block's MLP output, x): the
@@ -231,11 +231,12 @@ class Evo2DecoderLayer(nn.Module):
         sum the reference forms at the end of each block."""
         if self.kind != "attn" and getattr(self.mixer, "fuses_pre_norm", False):
             # pre-norm, residual add and the in_proj quantisation in one pass
-            m = (self.mixer(x, pre_norm=self.pre_norm) if add is None
-                 else self.mixer(add, pre_norm=self.pre_norm, residual=x))
+            m = (self.mixer(x, input_ids, pre_norm=self.pre_norm) if add is None
+                 else self.mixer(add, input_ids, pre_norm=self.pre_norm, residual=x))
         else:
             pre = self.pre_norm(x) if add is None else self.pre_norm.add_norm_(add, x)
-            m = self.mixer(pre, positions, segments) if self.kind == "attn" else self.mixer(pre)
+            m = (self.mixer(pre, positions, segments) if self.kind == "attn"
+                 else self.mixer(pre, input_ids))
         post = self.post_norm.add_norm_(m, x)  # x <- m + x
         return self.mlp(post), x
 
@@ -325,7 +326,7 @@ class StripedHyena2(nn.Module):
         add = None
         with set_forward_metadata(meta):
             for layer in self.layers:
-                add, x = layer(x, positions, segments, add)
+                add, x = layer(x, positions, segments, add, input_ids)
         return self.norm.add_norm_(add, x)
 
     def logprobs(self, h, targets):

@@ -246,6 +246,35 @@ def quant_e4m3(x, input_scale, out=None):
     return out
 
 
+def gemm_fp8_emulated(a, w_t, scale_a, scale_b, out=None):
+    """out (N, M) bf16 = Hopper fast-accumulation model of a (N, K) e4m3 . w_t (K, M)
+    (bf16 holding E4M3 values), scaled by sa then sb (fp8_emul.py:45-88)."""
+    _cuda(a, "a")
+    _require(a.dtype == E4M3 and a.dim() == 2 and a.stride(1) == 1, "a must be (N, K) e4m3 rows")
+    _require(w_t.dtype == BF16 and w_t.dim() == 2 and w_t.stride(1) == 1 and
+             w_t.shape[0] == a.shape[1], "w_t must be (K, M) bf16 rows")
+    N, K = a.shape
+    M = w_t.shape[1]
+    if out is None:
+        out = torch.empty(N, M, dtype=BF16, device=a.device)
+    lib = _lib.load()
+    _lib.check(lib.hyena_gemm_fp8_emulated(_ptr(a), a.stride(0), _ptr(w_t), w_t.stride(0),
+                                           _ptr(out), out.stride(0), N, M, K, _ptr(scale_a),
+                                           _ptr(scale_b), _stream()), "hyena_gemm_fp8_emulated")
+    return out
+
+
+def fp8_linear_emulated(x, w_t, scales):
+    """The FP8-surgery projection without FP8 hardware (mixers.py:701-705,
+    fp8_emul_triton.py:181-191): q(x) with the static input scale scales[0],
+    then the fast-accumulation model against w_t (K, M), times scales[0] * scales[1]."""
+    _require(scales.dtype == torch.float32 and scales.numel() == 2, "scales must be 2 fp32")
+    sx, sw = scales[0:1], scales[1:2]
+    x2 = x.reshape(-1, x.shape[-1])
+    q = quant_e4m3(x2.contiguous(), sx)
+    return gemm_fp8_emulated(q, w_t, sx, sw).reshape(*x.shape[:-1], w_t.shape[1])
+
+
 def rms_norm(x, weight, eps, residual=None, *, want_y=True, quant_scale=None, s_out=None):
     """Evo2RMSNorm of the decoder layer (model.py:47-76 Evo2RMSNorm.forward;
     triton_norm.py:127-156 rms_norm), one pass over the rows of x (M, H) bf16:

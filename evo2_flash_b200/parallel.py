@@ -51,6 +51,11 @@ def shard_mixer_tensors(tensors: dict, rank: int, world: int, hidden: int) -> di
             out[name] = t[rows]
         elif name == "log_poles":
             out[name] = t.reshape(hidden, -1, 1)[rows]
+        elif name in ("in_proj_token_table", "in_proj_emul_weight_t", "in_proj_emul_scales",
+                      "in_proj_emul_cols"):
+            if world != 1:  # FP8-surgery projections (mixers.py:758-800)
+                raise ValueError(f"{name}: FP8-surgery layers are not channel-sharded")
+            out[name] = t
         else:
             raise KeyError(f"unexpected mixer tensor {name!r}")
     return out

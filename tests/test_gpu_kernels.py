@@ -269,6 +269,37 @@ def test_quant_e4m3_exact():
     assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(ref))
 
 
+def test_emulated_fp8_gemm_matches_reference_fixture():
+    """The Hopper fast-accumulation model against the reference's own emulation
+    output (fp8_emul.static_fp8_linear_emulated, golden fixture): bit for bit."""
+    from evo2_flash_b200 import ops
+    from tests.helpers import load_fixture
+
+    fx = load_fixture("fp8_in_proj")
+    w8 = fx["w8"].view(torch.float8_e4m3fn)
+    w_t = w8.float().t().contiguous().to(torch.bfloat16)
+    scales = torch.stack([fx["sx"].reshape(()), fx["sw"].reshape(())]).float()
+    out = ops.fp8_linear_emulated(fx["x"].to(DEV), w_t.to(DEV), scales.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), fx["out_hopper"])
+
+
+@pytest.mark.parametrize("N,K,M", [(200, 512, 384), (1, 4096, 128), (37, 96, 70)])
+def test_emulated_fp8_gemm_matches_oracle(N, K, M):
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(N + K + M)
+    x = (torch.randn(N, K, generator=g) * torch.logspace(-2, 2, K)).to(torch.bfloat16)
+    x[0, :5] = 0.0
+    w8 = (torch.randn(M, K, generator=g) * 40).clamp(-448, 448).to(torch.float8_e4m3fn)
+    sx, sw = torch.tensor([0.05]), torch.tensor([0.01])
+    ref = O.fp8_linear(x, w8, sx, sw, hopper=True)
+    w_t = w8.float().t().contiguous().to(torch.bfloat16)
+    out = ops.fp8_linear_emulated(x.to(DEV), w_t.to(DEV), torch.cat([sx, sw]).to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), ref)
+
+
 def _all_finite_bf16(cols=512):
     """Every finite bf16 value once, as (rows, cols) rows (zero padded)."""
     x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)

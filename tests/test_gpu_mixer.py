@@ -105,3 +105,100 @@ def test_pre_norm_fused_into_the_in_proj_pass(name, fp8):
     assert torch.equal(outs[0][1], (add.cpu().float() + x0.cpu().float()).to(torch.bfloat16))
     assert torch.equal(outs[0][1], outs[1][1])
     assert torch.equal(outs[0][0], outs[1][0])
+
+
+def _surgery_mixer(fx, **flags):
+    from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer
+
+    cfg = SimpleNamespace(hidden_size=fx["H"], short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=False, vocab_size=512, **flags)
+    kw = dict(num_spec=fx["num_spec"], device=DEV)
+    if fx["kind"] == "hcl":
+        return HyenaIIRMixer(cfg, 0, prefix=fx["name"] + "_s", **kw)
+    return HyenaFIRMixer(cfg, 0, prefix=fx["name"] + "_s", k_inner=fx["k_inner"], **kw)
+
+
+@pytest.mark.parametrize("name", ["hcs_mixed", "hcl_mixed"])
+def test_token_table_layer(name):
+    """FP8-surgery token table (mixers.py:1079-1084): z is the table row of each
+    token, and the rest of the layer is the ordinary path (checked against the
+    oracle's mixer core on the same z)."""
+    from evo2_flash_b200 import set_forward_metadata
+    from oracle import hyena_oracle as O
+    from tests.helpers import empty_states, oracle_params
+
+    fx = load_fixture(name)
+    H = fx["H"]
+    m = _surgery_mixer(fx, hyena_token_table_layers=[0])
+    g = torch.Generator().manual_seed(8)
+    table = (torch.randn(512, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+    params = {k: v for k, v in fx["params"].items() if k != "in_proj.weight"}
+    params["in_proj_token_table"] = table
+    m.load_full_weights({k: v.to(DEV) for k, v in params.items()})
+    m.allocate_state(fx["num_blocks"], DEV)
+    step = fx["steps"][0]
+    T = step["x"].shape[0]
+    ids = torch.randint(0, 512, (T,), generator=g)
+    seen = {}
+    m.in_proj.register_forward_hook(lambda mod, a, o: seen.__setitem__("z", o[0]))
+    with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+        out = m(step["x"].to(DEV), ids.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(seen["z"].cpu(), table[ids])
+    p = oracle_params(fx)
+    ref = O.out_proj(O.mixer_core(table[ids], p, meta_from_dict(step["meta"]), empty_states(fx)), p)
+    assert max_rel_err(out.cpu(), ref) < REL_TOL
+    with pytest.raises(ValueError):
+        with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+            m(step["x"].to(DEV))  # a token table needs the token ids
+
+
+def test_emulated_and_hybrid_projections():
+    """Fully emulated (mixers.py:1085-1089) and hybrid (mixers.py:691-702)
+    FP8-surgery projections: z is the Hopper fast-accumulation model of the
+    oracle, bit for bit, on the emulated columns; the hybrid's other columns are
+    the bf16 projection."""
+    from evo2_flash_b200 import ops, set_forward_metadata
+    from oracle import hyena_oracle as O
+
+    fx = load_fixture("hcs_mixed")
+    H = fx["H"]
+    g = torch.Generator().manual_seed(9)
+    w8 = (torch.randn(3 * H, H, generator=g) * 60).clamp(-448, 448).to(torch.float8_e4m3fn)
+    sx, sw = torch.tensor([0.02]), torch.tensor([0.004])
+    step = fx["steps"][0]
+    x = step["x"]
+    z_emul = O.fp8_linear(x, w8, sx, sw, hopper=True)
+    w_t = w8.float().t().contiguous().to(torch.bfloat16)
+    scales = torch.cat([sx, sw])
+
+    m = _surgery_mixer(fx, hyena_fp8_emulated_layers=[0])
+    params = {k: v for k, v in fx["params"].items() if k != "in_proj.weight"}
+    params.update(in_proj_emul_weight_t=w_t, in_proj_emul_scales=scales)
+    m.load_full_weights({k: v.to(DEV) for k, v in params.items()})
+    m.allocate_state(fx["num_blocks"], DEV)
+    seen = {}
+    m.in_proj.register_forward_hook(lambda mod, a, o: seen.__setitem__("z", o[0]))
+    with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+        m(x.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(seen["z"].cpu(), z_emul)
+
+    cols = torch.tensor([0, 5, 17, 3 * H - 1, 40, 41, 2, 99])
+    m = _surgery_mixer(fx, hyena_fp8_emulated_channels={0: len(cols)})
+    params = dict(fx["params"])
+    params.update(in_proj_emul_weight_t=w_t[:, cols].contiguous(), in_proj_emul_scales=scales,
+                  in_proj_emul_cols=cols)
+    m.load_full_weights({k: v.to(DEV) for k, v in params.items()})
+    m.allocate_state(fx["num_blocks"], DEV)
+    seen = {}
+    m.in_proj.register_forward_hook(lambda mod, a, o: seen.__setitem__("z", o[0]))
+    with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+        m(x.to(DEV))
+    torch.cuda.synchronize()
+    z = seen["z"].cpu()
+    assert torch.equal(z[:, cols], z_emul[:, cols])
+    plain = ops.gemm_bf16(x.to(DEV), fx["params"]["in_proj.weight"].to(DEV), None).cpu()
+    keep = torch.ones(3 * H, dtype=torch.bool)
+    keep[cols] = False
+    assert torch.equal(z[:, keep], plain[:, keep])
