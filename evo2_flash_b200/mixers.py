@@ -32,10 +32,9 @@ import torch
 from torch import nn
 
 from . import ops
+from .custom_op import HYENA_MIXER_OP, register_layer
 from .forward_context import lookup
 from .parallel import PendingReduce, all_reduce_partial, all_reduce_partial_async, shard_mixer_tensors
-
-HYENA_MIXER_OP = "evo2_b200::hyena_mixer"
 
 
 # ---------------------------------------------------------------- projections
@@ -167,7 +166,8 @@ class HyenaMixerBase(nn.Module):
 
     def __init__(self, config, layer_idx: int, model_config=None, cache_config=None,
                  prefix: str = "", quant_config=None, *, num_spec: int | None = None,
-                 tp_rank: int = 0, tp_size: int = 1, tp_group=None, device=None):
+                 tp_rank: int = 0, tp_size: int = 1, tp_group=None, device=None,
+                 compilation_config=None):
         super().__init__()
         self.config = config
         self.layer_idx = layer_idx
@@ -232,6 +232,10 @@ class HyenaMixerBase(nn.Module):
         self.kv_cache = (torch.tensor([]), torch.tensor([]), torch.tensor([]))
         self._weights = None
         self._weights_key = None
+        # With an engine's compilation config the layer registers under its
+        # prefix and forward() runs as the opaque custom op (mixers.py:807-829).
+        register_layer(prefix, self, compilation_config)
+        self.use_custom_op = compilation_config is not None
 
     # ---- kernel-side weights --------------------------------------------------
     def _kernel_weights(self) -> ops.LayerWeights:
@@ -455,7 +459,13 @@ class HyenaMixerBase(nn.Module):
         With `pre_norm` (the decoder layer's Evo2RMSNorm: `.weight`, `.eps`) the
         mixer's input is pre_norm(hidden_states + residual) -- hidden_states
         alone without a residual -- computed in the in_proj's input pass; the
-        sum is written back into `residual`, as vLLM's fused add-RMSNorm does."""
+        sum is written back into `residual`, as vLLM's fused add-RMSNorm does.
+        A layer built with a compilation config runs the plain form through the
+        custom op torch.ops.evo2_b200.hyena_mixer."""
+        if self.use_custom_op and pre_norm is None:
+            output = torch.empty_like(hidden_states)
+            torch.ops.evo2_b200.hyena_mixer(hidden_states, output, token_ids, self.prefix)
+            return output
         return self._forward_impl(hidden_states, token_ids, pre_norm=pre_norm, residual=residual)
 
     def forward_async(self, hidden_states, token_ids=None, *, pre_norm=None,

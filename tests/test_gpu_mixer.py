@@ -202,3 +202,25 @@ def test_emulated_and_hybrid_projections():
     keep = torch.ones(3 * H, dtype=torch.bool)
     keep[cols] = False
     assert torch.equal(z[:, keep], plain[:, keep])
+
+
+def test_forward_through_the_custom_op_matches_direct():
+    """A mixer built with an engine compilation config runs forward() as
+    torch.ops.evo2_b200.hyena_mixer; the result equals the direct call."""
+    from evo2_flash_b200 import HyenaFIRMixer, set_forward_metadata
+
+    fx = load_fixture("hcm_prefill")
+    comp = SimpleNamespace(static_forward_context={}, splitting_ops=[])
+    cfg = SimpleNamespace(hidden_size=fx["H"], short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=False)
+    outs = []
+    for i, cc in enumerate((comp, None)):
+        m = HyenaFIRMixer(cfg, 0, prefix=f"op_test_{i}", k_inner=fx["k_inner"], device=DEV,
+                          compilation_config=cc)
+        m.load_full_weights({k: v.to(DEV) for k, v in fx["params"].items()})
+        m.allocate_state(fx["num_blocks"], DEV)
+        step = fx["steps"][0]
+        with set_forward_metadata(meta_from_dict(step["meta"], DEV)):
+            outs.append(m(step["x"].to(DEV)).cpu())
+    assert torch.equal(outs[0], outs[1])
+    assert max_rel_err(outs[0], fx["steps"][0]["out"]) < REL_TOL
