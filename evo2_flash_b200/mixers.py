@@ -272,6 +272,29 @@ class HyenaMixerBase(nn.Module):
                               for s, d in zip(shapes, dtypes))
         return self.kv_cache
 
+    # ---- engine surface (vLLM MambaBase; mixers.py:832-850) -------------------
+    attn_backend = None  # the engine's metadata backend class; None: vLLM's stock Mamba2
+
+    @property
+    def mamba_type(self):
+        """MAMBA2: the metadata builder that passes accepted-token counts
+        (mixers.py:833-840); the string "mamba2" without vLLM."""
+        try:
+            from vllm.v1.attention.backends.registry import MambaAttentionBackendEnum
+        except Exception:  # vLLM absent: engine-free use
+            return "mamba2"
+        return MambaAttentionBackendEnum.MAMBA2
+
+    def get_attn_backend(self):
+        """The metadata backend (mixers.py:842-850): `attn_backend` when set (with
+        speculation the engine's Hyena builder, which adds num_computed_tokens_d;
+        the mixers read the same field names), else vLLM's stock Mamba2 one."""
+        if self.attn_backend is not None:
+            return self.attn_backend
+        from vllm.v1.attention.backends.mamba2_attn import Mamba2AttentionBackend
+
+        return Mamba2AttentionBackend
+
     @staticmethod
     def decode_state_indices(m):
         idx = m.state_indices_tensor_d

@@ -53,3 +53,25 @@ def test_engine_config_registration():
     assert comp.splitting_ops == [HYENA_MIXER_OP]
     with pytest.raises(ValueError):
         HyenaFIRMixer(cfg, 1, prefix="model.layers.0.mixer", k_inner=7, compilation_config=comp)
+
+
+def test_engine_state_surface():
+    """get_state_shape / get_state_dtype / mamba_type / get_attn_backend, the
+    MambaBase surface vLLM builds the paged state from (mixers.py:832-917)."""
+    from evo2_flash_b200.mixers import HyenaIIRMixer
+
+    cfg = SimpleNamespace(hidden_size=64, short_filter_length=3, hcm_filter_length=128,
+                          state_size=16, use_fp8_input_projections=False)
+    m = HyenaIIRMixer(cfg, 0, prefix="surface.mixer", num_spec=3)
+    assert m.get_state_shape() == ((2 + 3, 192), (127, 64), (64, 17))
+    assert m.get_state_dtype() == (torch.bfloat16, torch.float32, torch.float32)
+    try:
+        from vllm.v1.attention.backends.mamba2_attn import Mamba2AttentionBackend
+        from vllm.v1.attention.backends.registry import MambaAttentionBackendEnum
+    except Exception:
+        assert m.mamba_type == "mamba2"
+        return
+    assert m.mamba_type == MambaAttentionBackendEnum.MAMBA2
+    assert m.get_attn_backend() is Mamba2AttentionBackend
+    m.attn_backend = object
+    assert m.get_attn_backend() is object
