@@ -75,6 +75,37 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     return;
   }
 
+  // LI with contiguous modes: the warp's state run (32 channels x D floats of
+  // the snapshot block) is put in flight now, into shared memory with
+  // cp.async, and read after the short filter (see the staged path below).
+  constexpr bool kIIR = KIND == HYENA_KIND_IIR;
+  __shared__ float stage_sm[kIIR ? DEC_THREADS / 32 : 1][kIIR ? 32 * (IIR_STAGE_MAXD + 1) : 1];
+  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
+  const bool src_ok = block_ok(src, A.inner_state);
+  const long long Dst = A.inner_state.dim_stride;
+  const bool staged = kIIR && A.inner_state.col_stride == 1 && Dst >= 16 && Dst <= IIR_STAGE_MAXD;
+  if constexpr (kIIR) {
+    if (staged) {
+      const int lane = threadIdx.x & 31;
+      float* w = stage_sm[threadIdx.x >> 5];
+      const int D = (int)Dst, pitch = D | 1;  // odd row pitch: conflict-free row reads
+      const long long h0 = (long long)(h - lane);  // the warp's first channel
+      const float* sp = static_cast<const float*>(A.inner_state.data) +
+                        src * A.inner_state.block_stride + h0 * Dst;
+      for (int j = lane; j < 32 * D; j += 32) {
+        float* d = &w[(j / D) * pitch + j % D];
+        if (src_ok)
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                           static_cast<uint32_t>(__cvta_generic_to_shared(d))),
+                       "l"(sp + j)
+                       : "memory");
+        else
+          *d = 0.0f;
+      }
+      cp_async_commit();
+    }
+  }
+
   // ---- short filter on the triple, window shift
   const int W0 = A.conv_state.cols;
   bf16* s0 = static_cast<bf16*>(A.conv_state.data);
@@ -127,7 +158,6 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   for (int p = 0; p < DEC_MAXQ; ++p) u[p] = bf16r(xs[1][p] * xs[2][p]);
 
   // ---- inner operator with snapshots
-  const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
   long long dst[DEC_MAXQ];
   bool dok[DEC_MAXQ];
 #pragma unroll
@@ -136,7 +166,6 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     dok[p] = p < n && block_ok(dst[p], A.inner_state) &&
              !(A.skip_null_writes && dst[p] == A.null_block);
   }
-  const bool src_ok = block_ok(src, A.inner_state);
   if (!src_ok && threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
   float y[DEC_MAXQ];
 #pragma unroll
@@ -197,18 +226,14 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     // the state and every snapshot move through shared memory with coalesced
     // 4-byte accesses (the stamp column is never written) instead of 16
     // scattered ones per thread.
-    const long long D = A.inner_state.dim_stride;
-    const bool staged = cs == 1 && D >= 16 && D <= IIR_STAGE_MAXD;
+    const long long D = Dst;
     if (staged) {
-      __shared__ float sm[DEC_THREADS / 32][32 * (IIR_STAGE_MAXD + 1)];
       const int lane = threadIdx.x & 31;
-      float* w = sm[threadIdx.x >> 5];
+      float* w = stage_sm[threadIdx.x >> 5];
       const long long h0 = (long long)(h - lane);  // the warp's first channel
-      const int pitch = (int)(D | 1);  // odd row pitch: conflict-free row reads
+      const int pitch = (int)(D | 1);
       const int run = 32 * (int)D;
-      const float* sp = st + src * A.inner_state.block_stride + h0 * D;
-      for (int j = lane; j < run; j += 32)
-        w[(j / (int)D) * pitch + j % (int)D] = src_ok ? sp[j] : 0.0f;
+      cp_async_wait<0>();  // the state run put in flight before the short filter
       __syncwarp();
 #pragma unroll
       for (int q = 0; q < 16; ++q) s[q] = w[lane * pitch + q];
