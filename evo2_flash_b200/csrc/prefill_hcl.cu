@@ -121,8 +121,9 @@ __device__ __forceinline__ void split_triples_hcl(uint32_t w0, uint32_t w1, uint
 
 // Walks the chunk's rows in tiles: all threads stage the z rows and run the K=3
 // filter + gate on channel pairs (bf16x2), then fn(row, x2, u) is called in row
-// order with this thread's channel.
-template <typename F>
+// order with this thread's channel.  NEED_X2 = false (the aggregate pass, which
+// uses u only) skips the x2 column's filter; fn then gets x2 = 0.
+template <bool NEED_X2, typename F>
 __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
                                            const hyena_layer_params& P, const ChunkCtx& c,
                                            int c0, HclTile& S, F&& fn) {
@@ -187,13 +188,13 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
           split_triples_hcl(zt[row][3 * pp], zt[row][3 * pp + 1], zt[row][3 * pp + 2],
                             cur[0], cur[1], cur[2]);
 #pragma unroll
-          for (int col = 0; col < 3; ++col) {
+          for (int col = NEED_X2 ? 0 : 1; col < 3; ++col) {
             o[col] = short_tap2(h2[col], h1[col], cur[col], w[col][0], w[col][1], w[col][2]);
             h2[col] = h1[col];
             h1[col] = cur[col];
           }
           S.ug[row][pp] = __hmul2(o[1], o[2]);
-          S.x2g[row][pp] = o[0];
+          if constexpr (NEED_X2) S.x2g[row][pp] = o[0];
         }
       }
     }
@@ -207,7 +208,7 @@ __device__ __forceinline__ void walk_chunk(const hyena_prefill_args& A,
     const bf16* ug = reinterpret_cast<const bf16*>(&S.ug[0][0]);
     const bf16* xg = reinterpret_cast<const bf16*>(&S.x2g[0][0]);
     for (int row = 0; row < n; ++row)
-      fn(t0 + row, ldbf(xg + row * HCL_CG + tid), ldbf(ug + row * HCL_CG + tid));
+      fn(t0 + row, NEED_X2 ? ldbf(xg + row * HCL_CG + tid) : 0.0f, ldbf(ug + row * HCL_CG + tid));
     __syncthreads();
   }
   cp_async_wait<0>();
@@ -248,7 +249,7 @@ hcl_aggregate_kernel(const hyena_layer_params P, const hyena_prefill_args A, Hcl
   load_pole_pairs(P, h, p2);
 #pragma unroll
   for (int i = 0; i < HCL_S / 2; ++i) acc[i] = 0ull;
-  walk_chunk(A, P, c, c0, S, [&](int, float, float u) {
+  walk_chunk<false>(A, P, c, c0, S, [&](int, float, float u) {
     const f2 uu = f2_make(u, u);
 #pragma unroll
     for (int i = 0; i < HCL_S / 2; ++i) acc[i] = f2_add(f2_mul(acc[i], p2[i]), uu);
@@ -318,7 +319,7 @@ hcl_output_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWor
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float d = Dg ? ldbf(Dg + h) : 0.0f;
   bf16* out = static_cast<bf16*>(A.out);
-  walk_chunk(A, P, c, c0, S, [&](int row, float x2, float u) {
+  walk_chunk<true>(A, P, c, c0, S, [&](int row, float x2, float u) {
     const f2 uu = f2_make(u, u);
 #pragma unroll
     for (int i = 0; i < HCL_S / 2; ++i) s2[i] = f2_add(f2_mul(s2[i], p2[i]), uu);
