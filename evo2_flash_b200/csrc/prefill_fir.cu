@@ -355,6 +355,11 @@ prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
   }
   bf16* s0 = static_cast<bf16*>(A.conv_state.data);
   const bf16* z = static_cast<const bf16*>(A.z);
+  // blockIdx.z splits the K-1 history positions when every one of them comes
+  // from this segment's own z rows (L >= K+1: no old window is read, so the
+  // split blocks are independent); otherwise block z = 0 does all of them, in
+  // the in-place order below.  Only block z = 0 reads and rewrites S0.
+  const int zi = (int)blockIdx.z;
 
   // Old S0 columns 0..1 for the three z columns of channel h (read before any write).
   float old0[3][2];
@@ -362,7 +367,7 @@ prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
   for (int q = 0; q < 3; ++q)
 #pragma unroll
     for (int i = 0; i < 2; ++i)
-      old0[q][i] = seg.init ? ldbf(s0 + seg.blk * A.conv_state.block_stride +
+      old0[q][i] = seg.init && zi == 0 ? ldbf(s0 + seg.blk * A.conv_state.block_stride +
                                    (long long)i * A.conv_state.col_stride +
                                    (long long)(3 * h + q) * A.conv_state.dim_stride)
                             : 0.0f;
@@ -378,7 +383,11 @@ prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
       w2[q] = ldbf(sw + (3 * h + 2) * 3 + q);
     }
     float* base = s1 + seg.blk * A.inner_state.block_stride + (long long)h * A.inner_state.dim_stride;
-    for (int i = 0; i < HIST; ++i) {
+    const bool split = L >= HIST + 2;
+    const int chunk = (HIST + (int)gridDim.z - 1) / (int)gridDim.z;
+    const int i0 = split ? zi * chunk : (zi == 0 ? 0 : HIST);
+    const int i1 = split ? min(HIST, i0 + chunk) : HIST;
+    for (int i = i0; i < i1; ++i) {
       const int src = L + i;  // position in concat(hist[HIST], u[L])
       float val;
       if (src < HIST) {
@@ -410,6 +419,7 @@ prefill_state_kernel(const hyena_layer_params P, const hyena_prefill_args A) {
   }
 
   // New S0 columns 0..1.
+  if (zi != 0) return;
 #pragma unroll
   for (int q = 0; q < 3; ++q) {
 #pragma unroll
@@ -439,7 +449,7 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   launch_kernel(fir_prefill_kernel<K>, dim3(grid), dim3(FIR_THREADS), smem, st, 0u, P, A, rows);
   int rc = check_launch("fir_prefill_kernel");
   if (rc) return rc;
-  dim3 g2(A.num_segments, (P.H + 127) / 128);
+  dim3 g2(A.num_segments, (P.H + 127) / 128, K > 16 ? 8 : 1);
   launch_kernel(prefill_state_kernel<K>, dim3(g2), dim3(128), 0, st, 0u, P, A);
   return check_launch("prefill_state_kernel");
 }
