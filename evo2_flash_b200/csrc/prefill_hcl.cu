@@ -284,12 +284,21 @@ hcl_carry_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclWork
   const float pc = expf(P.log_poles[(long long)h * P.lp_stride_h + s * P.lp_stride_s] * (float)HCL_C);
   float* slot = W.states + (long long)base * P.H * HCL_S + idx;
   const long long stride = (long long)P.H * HCL_S;
-  float a = nch > 1 ? slot[0] : 0.0f;
-  for (int k = 0; k < nch; ++k) {
-    const float next = (k + 1 < nch - 1) ? slot[(k + 1) * stride] : 0.0f;  // prefetch
-    slot[k * stride] = S;
-    if (k < nch - 1) S = add_rn(mul_rn(pc, S), a);
-    a = next;
+  // Eight chunks per round: their aggregates are loaded together (every slot
+  // is read before this thread overwrites it), then the carry runs through
+  // them in order.  The last chunk's aggregate is never read.
+  constexpr int CB = 8;
+  for (int k0 = 0; k0 < nch; k0 += CB) {
+    float a[CB];
+#pragma unroll
+    for (int u = 0; u < CB; ++u) a[u] = (k0 + u < nch - 1) ? slot[(k0 + u) * stride] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < CB; ++u) {
+      const int k = k0 + u;
+      if (k >= nch) break;
+      slot[k * stride] = S;
+      if (k < nch - 1) S = add_rn(mul_rn(pc, S), a[u]);
+    }
   }
 }
 
