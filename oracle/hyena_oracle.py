@@ -29,8 +29,6 @@ State layout (vLLM's SD orientation, mixers.py:940-949): conv state
 
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn.functional as F
 

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from oracle import hyena_oracle as O
-from tests.helpers import (REL_TOL, empty_states, load_fixture, max_rel_err, meta_from_dict,
+from tests.helpers import (empty_states, load_fixture, max_rel_err, meta_from_dict,
                            oracle_params, record_stamps, spec_accepted)
 
 CASES = ["hcm_prefill", "hcs_mixed", "hcl_mixed", "hcm_decode", "hcm_spec", "hcl_spec", "hcs_spec"]
