@@ -55,7 +55,7 @@ METRIC = "Hyena-mixer prefill+decode tok/s/GPU at 7B shape; % HBM / fp8 tensor r
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes (read + write) of one in_proj GEMM launch per token, from an ncu
 # capture of the T = 16384 case (dram__bytes_read.sum + dram__bytes_write.sum =
-# 269350912 + 377080576 B; profiles/gemm_tcgen05_prefill_7b.md), scaled by T
+# 269350912 + 377080576 B), scaled by T
 IN_PROJ_DRAM_BYTES_PER_TOKEN = (269350912 + 377080576) / 16384
 
 

@@ -13,7 +13,7 @@ from ._build import LIB_PATH
 
 HYENA_KIND_FIR = 0
 HYENA_KIND_IIR = 1
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class StateView(C.Structure):
@@ -61,6 +61,14 @@ class PrefillArgs(C.Structure):
         ("conv_state", StateView),
         ("inner_state", StateView),
         ("error_flags", C.c_void_p),
+    ]
+
+
+class StateBlock(C.Structure):
+    _fields_ = [
+        ("data", C.c_void_p),
+        ("block_stride_bytes", C.c_int64),
+        ("block_bytes", C.c_int64),
     ]
 
 
@@ -118,10 +126,18 @@ SIGNATURES = {
                                           C.c_void_p, C.c_void_p, C.c_void_p]),
     "hyena_gemm_workspace_size": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     "hyena_set_gemm_max_ctas": (None, [C.c_int32]),
+    "hyena_gemm_wait_timeouts": (C.c_int, [C.POINTER(C.c_int32), C.c_int32]),
     "hyena_set_launch_chaining": (None, [C.c_int32]),
     "hyena_spec_accepted": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p]),
+    "hyena_spec_record_prefill": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
+                                            C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
+                                            C.c_void_p]),
+    "hyena_state_repair": (C.c_int, [C.c_int32, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                     C.POINTER(StateBlock), C.c_int32, C.c_void_p, C.c_void_p,
+                                     C.c_void_p]),
     "hyena_spec_record": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
                                     C.c_void_p, C.c_void_p]),

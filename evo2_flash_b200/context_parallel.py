@@ -50,18 +50,37 @@ def _segment_meta(n, device, init):
         seq_lens=torch.tensor([n], dtype=torch.int32, device=device))
 
 
-def li_entry_state(finals: torch.Tensor, log_poles: torch.Tensor, slice_len: int,
-                   rank: int) -> torch.Tensor:
+def li_entry_state(finals: torch.Tensor, log_poles: torch.Tensor, slice_lens, rank: int
+                   ) -> torch.Tensor:
     """State entering slice `rank` from every slice's zero-start final state.
 
-    finals (P, H, S) fp32: A_q; log_poles (H, S[, 1]).  S_r = p^L S_{r-1} +
-    A_{r-1}, S_0 = 0, with p^L = exp(L log p) in fp32."""
+    finals (P, H, S) fp32: A_q; log_poles (H, S[, 1]); slice_lens: the token
+    count of every slice (a sequence of P ints, or one int when all are equal).
+    S_r = p^(L_{r-1}) S_{r-1} + A_{r-1}, S_0 = 0, with p^L = exp(L log p) in fp32:
+    the state leaving slice q is its own A_q plus the entering state carried
+    over that slice's own length."""
+    P = finals.shape[0]
+    lens = [int(slice_lens)] * P if isinstance(slice_lens, int) else [int(n) for n in slice_lens]
+    if len(lens) != P:
+        raise ValueError(f"{len(lens)} slice lengths for {P} slices")
     lp = log_poles.reshape(finals.shape[1], finals.shape[2]).float()
-    pl = torch.exp(lp * float(slice_len))
     s = torch.zeros_like(finals[0])
     for q in range(rank):
-        s = pl * s + finals[q]
+        s = torch.exp(lp * float(lens[q])) * s + finals[q]
     return s
+
+
+def pack_final(final: torch.Tensor, slice_len: int) -> torch.Tensor:
+    """(H + 1, S): a slice's final state with its token count in the extra row,
+    so that one all-gather carries both (the count is exact in fp32 below 2^24)."""
+    row = torch.full((1, final.shape[1]), float(slice_len), dtype=final.dtype,
+                     device=final.device)
+    return torch.cat([final, row])
+
+
+def unpack_finals(packed: torch.Tensor):
+    """(P, H + 1, S) gathered pack_final rows -> ((P, H, S) finals, [L_q])."""
+    return packed[:, :-1], [int(v) for v in packed[:, -1, 0].tolist()]
 
 
 def dist_gather(group=None):
@@ -75,25 +94,29 @@ def dist_gather(group=None):
 
 
 class LiSlice:
-    """An LI layer's slice between the two passes: `local_final` (H, S) is A_r,
-    to be gathered over the ranks; finish(finals) runs pass 2."""
+    """An LI layer's slice between the two passes: `local_final` (H + 1, S) is
+    A_r with this slice's token count in its last row (pack_final), to be
+    gathered over the ranks; finish(gathered) runs pass 2."""
 
     def __init__(self, mixer, zl, meta, window, rank, g):
         self.mixer, self.zl, self.meta, self.window, self.rank = mixer, zl, meta, window, rank
         conv, inner = mixer._states_for_kernels()
-        self.local_final = inner[1, :, :mixer.state_size].clone()
+        self.local_final = pack_final(inner[1, :, :mixer.state_size], zl.shape[0])
         # slice 0 enters with the zero state: its pass 1 is already exact
         self._out = mixer._out_proj(g) if rank == 0 else None
 
-    def finish(self, finals: torch.Tensor) -> torch.Tensor:
+    def finish(self, gathered: torch.Tensor) -> torch.Tensor:
         if self._out is not None:
             return self._out
         m = self.mixer
+        finals, lens = unpack_finals(gathered)
+        if lens[self.rank] != self.zl.shape[0]:
+            raise RuntimeError(f"slice {self.rank}: gathered length {lens[self.rank]} != "
+                               f"{self.zl.shape[0]} (ranks gathered out of order)")
         conv, inner = m._states_for_kernels()
         with torch.no_grad():
             conv[1, :2] = self.window
-            inner[1, :, :m.state_size] = li_entry_state(finals, m.log_poles, self.zl.shape[0],
-                                                        self.rank)
+            inner[1, :, :m.state_size] = li_entry_state(finals, m.log_poles, lens, self.rank)
         g = m._run_core(self.zl, self.meta, None)  # pass 2: from S_r -> exact outputs
         return m._out_proj(g)
 
@@ -140,7 +163,8 @@ def cp_prefill(mixer, x_local: torch.Tensor, x_halo: torch.Tensor | None, rank: 
     this slice's hidden states; x_halo: the previous slice's last rows (at
     least halo_rows(mixer); None on rank 0).  gather(t) -> (P, ...) stacks a
     tensor over the ranks in rank order (default: dist_gather()); the LI layer
-    calls it once on every rank.  All slices must have the same length L."""
+    calls it once on every rank.  Slices may differ in length: each rank's
+    token count travels with its final state in the one all-gather."""
     r = cp_prefill_start(mixer, x_local, x_halo, rank)
     if isinstance(r, torch.Tensor):
         return r

@@ -43,6 +43,7 @@ int gemm_fp8_emulated_launch(const void* A, int64_t lda, const void* B, int64_t 
                              int64_t ldo, int N, int M, int K, const float* sa, const float* sb,
                              cudaStream_t st);
 void gemm_set_max_ctas(int n);
+int gemm_wait_timeouts(int32_t* count, int reset);
 int spec_accepted_launch(const int32_t* slots, int64_t slot_stride, int num_reqs,
                          const int32_t* computed, const float* stamps, int64_t stamp_stride,
                          int num_blocks, int num_spec, int32_t* accepted, int32_t* error_flags,
@@ -51,6 +52,14 @@ int spec_record_launch(const int32_t* out_slots, int64_t s0, int64_t s1, int num
                        const int32_t* starts, const int32_t* computed, float* stamps,
                        int64_t stamp_stride, int num_blocks, int32_t* error_flags,
                        cudaStream_t st);
+
+int state_repair_launch(int num_rows, const int32_t* dst, int64_t dst_stride, const int32_t* src,
+                        const int32_t* computed, const uint8_t* has_init, const float* stamps,
+                        int64_t stamp_stride, int num_blocks, const hyena_state_block* slices,
+                        int num_slices, int32_t* take, int32_t* error_flags, cudaStream_t st);
+int spec_record_prefill_launch(const int32_t* blocks, int64_t block_stride, int n,
+                               const int32_t* seq_lens, float* stamps, int64_t stamp_stride,
+                               int num_blocks, int32_t* error_flags, cudaStream_t st);
 
 static int check_params(const hyena_layer_params* p) {
   HB_REQUIRE(p != nullptr, "null layer params");
@@ -102,6 +111,24 @@ int hyena_spec_record(const int32_t* out_slots, int64_t s0, int64_t s1, int32_t 
   return hb::spec_record_launch(out_slots, s0, s1, num_reqs, q, starts, computed, stamps,
                                 stamp_stride, num_blocks, error_flags,
                                 static_cast<cudaStream_t>(stream));
+}
+
+int hyena_spec_record_prefill(const int32_t* blocks, int64_t block_stride, int32_t n,
+                              const int32_t* seq_lens, float* stamps, int64_t stamp_stride,
+                              int32_t num_blocks, int32_t* error_flags, void* stream) {
+  return hb::spec_record_prefill_launch(blocks, block_stride, n, seq_lens, stamps, stamp_stride,
+                                        num_blocks, error_flags,
+                                        static_cast<cudaStream_t>(stream));
+}
+
+int hyena_state_repair(int32_t num_rows, const int32_t* dst_blocks, int64_t dst_stride,
+                       const int32_t* src_blocks, const int32_t* computed,
+                       const uint8_t* has_init, const float* stamps, int64_t stamp_stride,
+                       int32_t num_blocks, const hyena_state_block* slices, int32_t num_slices,
+                       int32_t* take, int32_t* error_flags, void* stream) {
+  return hb::state_repair_launch(num_rows, dst_blocks, dst_stride, src_blocks, computed, has_init,
+                                 stamps, stamp_stride, num_blocks, slices, num_slices, take,
+                                 error_flags, static_cast<cudaStream_t>(stream));
 }
 
 void hyena_set_launch_chaining(int32_t enable) {
@@ -196,6 +223,11 @@ int hyena_gemm_fp8_emulated(const void* A, int64_t lda, const void* B, int64_t l
                             const float* scale_b, void* stream) {
   return hb::gemm_fp8_emulated_launch(A, lda, B, ldb, out, ldo, N, M, K, scale_a, scale_b,
                                       static_cast<cudaStream_t>(stream));
+}
+
+int hyena_gemm_wait_timeouts(int32_t* count, int32_t reset) {
+  HB_REQUIRE(count != nullptr, "hyena_gemm_wait_timeouts: null count");
+  return gemm_wait_timeouts(count, reset);
 }
 
 size_t hyena_gemm_workspace_size(int32_t M, int32_t N, int32_t K, int32_t fp8) {

@@ -22,7 +22,9 @@
 // partials over DSMEM in a fixed order (deterministic; no workspace, no atomics,
 // no second launch).
 // Every mbarrier wait is bounded by a globaltimer budget; on expiry the kernel
-// records the event in a device counter and runs to completion (TMEM freed).
+// records the event in a device counter and runs to completion (TMEM freed);
+// hyena_gemm_wait_timeouts reads the counter back, so a GEMM that gave up
+// (and wrote an incomplete tile) is reported instead of passing silently.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -931,6 +933,23 @@ int gemm_bf16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, voi
 }
 
 void gemm_set_max_ctas(int n) { gemm::g_max_ctas.store(n > 0 ? n : 0, std::memory_order_relaxed); }
+
+// Expired mbarrier waits counted on the current device since the last reset
+// (a synchronous copy of the device counter; not for use inside a capture).
+int gemm_wait_timeouts(int32_t* count, int reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, gemm::g_wait_timeouts, sizeof(int));
+  if (e != cudaSuccess)
+    return fail(HYENA_ERR_CUDA, std::string("gemm wait counter read: ") + cudaGetErrorString(e));
+  if (reset && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(gemm::g_wait_timeouts, &zero, sizeof(int));
+    if (e != cudaSuccess)
+      return fail(HYENA_ERR_CUDA, std::string("gemm wait counter reset: ") + cudaGetErrorString(e));
+  }
+  *count = v;
+  return HYENA_OK;
+}
 
 size_t gemm_workspace_size(int M, int N, int K, bool fp8) {
   (void)M;

@@ -17,7 +17,10 @@
 //     than ~32K packed tokens at H = 4096) is rejected with HYENA_ERR_INVALID;
 //   * the first call on a device looks the array's device address up (once per
 //     device, with that device current); make that first call before any
-//     stream capture;
+//     stream capture.  The address is cached per device ordinal for the life of
+//     the process and belongs to that device's primary context (the one the
+//     CUDA runtime uses): callers that make another context current, or reset
+//     the device (cudaDeviceReset), must not use this entry point afterwards;
 //   * every call shares the one array and leaves its contents behind: nothing in
 //     it needs to start at zero (the chunk table and every carried state are
 //     written before they are read), but two calls whose kernels overlap on the

@@ -28,6 +28,8 @@ partial outputs before the bias.  State shapes shrink to the local H.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 from torch import nn
 
@@ -59,7 +61,8 @@ class Fp8InProj(nn.Module):
 
 
 class Bf16Linear(nn.Module):
-    """bf16 nn.Linear on the tcgen05 GEMM.  forward -> (y, None)."""
+    """bf16 nn.Linear on the tcgen05 GEMM.  forward(x[, out=]) -> (y, None);
+    `out` (rows of x, N) receives the result in place of a new tensor."""
 
     def __init__(self, in_features, out_features, bias=False, device=None):
         super().__init__()
@@ -68,11 +71,13 @@ class Bf16Linear(nn.Module):
                                                device=device), requires_grad=False)
         self.bias = (nn.Parameter(torch.zeros(out_features, dtype=torch.bfloat16, device=device),
                                   requires_grad=False) if bias else None)
-        self.skip_bias = False  # the row-parallel out_proj adds it after the all-reduce
+        # A row-parallel out_proj adds its bias on one rank only (in that rank's
+        # GEMM epilogue), so the all-reduce of the partials counts it once.
+        self.skip_bias = False
 
-    def forward(self, x):
+    def forward(self, x, out=None):
         bias = None if self.skip_bias else self.bias
-        return ops.gemm_bf16(x, self.weight, bias), None
+        return ops.gemm_bf16(x, self.weight, bias, out=out), None
 
 
 class ProjectionTap(nn.Module):
@@ -97,65 +102,101 @@ class HybridProjection(Bf16Linear):
         return z.index_copy(-1, cols, emul), None
 
 
-# ---------------------------------------------------------------- helpers
-def _cache_safe_state_indices(indices, state):
-    """vLLM's undersized profiling cache: use null block 0 (mixers.py:527-540)."""
-    if indices.dim() == 2 and state.shape[0] < indices.numel():
-        return torch.zeros_like(indices)
-    return indices
+# ---------------------------------------------------------------- decode plan
+@dataclass
+class DecodePlan:
+    """Where the decode rows of one step read and write their state, resolved
+    on the device from the engine's metadata without a host synchronisation.
+
+    table     (reqs, cols) block table of the decode requests (a 1-D table is
+              one column); in the speculative layout column p is the snapshot
+              slot of verifier position p
+    in_slots  (reqs, q) blocks the inner state is read from, indexed by the
+              accepted count - 1
+    out_slots (reqs, q) blocks the state after token p is written to
+    starts    (reqs + 1,) token offsets of the requests, or None (one each)
+    conv_in / conv_out  (reqs,) blocks of the short-filter window
+    engine_accepted     the engine's own accepted counts (>= 1), or None when
+                        it sent none (the kernels then read every count as 1)
+    """
+
+    reqs: int
+    table: torch.Tensor
+    in_slots: torch.Tensor
+    out_slots: torch.Tensor
+    starts: torch.Tensor | None
+    conv_in: torch.Tensor
+    conv_out: torch.Tensor
+    engine_accepted: torch.Tensor | None
 
 
-def _accepted_tokens(m, num_reqs, device):
-    a = getattr(m, "num_accepted_tokens", None)
-    if a is None:
-        return torch.ones(num_reqs, device=device, dtype=torch.long)
-    if a.numel() < num_reqs:
-        raise ValueError(f"num_accepted_tokens is too short: shape={tuple(a.shape)}, "
-                         f"num_decodes={num_reqs}")
-    return a[:num_reqs].to(torch.long).clamp_min(1)
+def _profiling_table(table, num_blocks):
+    """vLLM's memory-profiling pass sizes the state cache for one block per
+    request while a speculative block table names one block per verifier
+    position; a table that cannot fit the cache is that pass (its results are
+    discarded), and it is pointed at the null block 0 instead.  Decided on
+    shapes alone, so it costs no synchronisation and is fixed under capture
+    (the reference's rule, mixers.py:527-540)."""
+    if table.dim() == 2 and table.numel() > num_blocks:
+        return table.new_zeros(table.shape)
+    return table
 
 
-def _decode_tensors(m, num_tokens, max_positions=None, accepted=None):
-    """(in_slots, out_slots, starts, accepted) on device (mixers.py:459-524),
-    including the prefix-caching ("all" mode) slot gathers (mixers.py:443-456).
-    accepted=False skips the accepted counts (returned as None)."""
-    slots = m.state_indices_tensor_d
-    if slots.dim() == 1:
-        slots = slots[:, None]
-    if slots.dim() != 2:
-        raise ValueError(f"state_indices_tensor_d must be rank 1 or 2, got shape={tuple(slots.shape)}")
-    num_reqs = int(m.num_decodes)
-    if slots.shape[0] < num_reqs:
-        raise ValueError(f"decode state rows={slots.shape[0]} smaller than num_decodes={num_reqs}")
+def _pick_columns(table, first_col, width):
+    """(reqs, width) columns of `table` starting at each request's first_col."""
+    cols = first_col[:, None].long() + torch.arange(width, device=table.device)
+    return table.gather(1, cols)
+
+
+def plan_decode(m, positions, num_blocks):
+    """DecodePlan of a step's decode rows (mixers.py:443-524 resolve the same
+    slots).  positions: verifier positions per request (1 + num_spec).
+    num_blocks: blocks of the smallest state slice (for the profiling rule).
+    Shape errors raise ValueError before anything is indexed; value ranges are
+    the engine's (out-of-range blocks are reported by the kernels' error word)."""
+    reqs = int(m.num_decodes)
+    tokens = int(m.num_decode_tokens)
+    table = m.state_indices_tensor_d
+    if table.dim() not in (1, 2):
+        raise ValueError(f"decode block table must be 1-D or 2-D, got {table.dim()}-D "
+                         f"{tuple(table.shape)}")
+    if table.dim() == 1:
+        table = table.unsqueeze(1)
+    if table.shape[0] < reqs:
+        raise ValueError(f"decode block table has {table.shape[0]} rows for {reqs} requests")
+    table = table[:reqs]
     starts = getattr(m, "query_start_loc_d", None)
-    if starts is None:
-        if num_tokens != num_reqs:
-            raise ValueError("packed multi-token decode requires query_start_loc_d: "
-                             f"num_decode_tokens={num_tokens}, num_decodes={num_reqs}")
-        starts = torch.arange(num_reqs + 1, device=slots.device, dtype=torch.int32)
+    if starts is not None:
+        if starts.numel() <= reqs:
+            raise ValueError(f"query_start_loc_d holds {starts.numel()} offsets, "
+                             f"{reqs + 1} needed")
+        starts = starts[: reqs + 1]
+    elif tokens != reqs:
+        raise ValueError(f"{tokens} decode tokens over {reqs} requests need query_start_loc_d "
+                         "(the per-request token offsets)")
+    engine = getattr(m, "num_accepted_tokens", None)
+    if engine is not None:
+        if engine.numel() < reqs:
+            raise ValueError(f"num_accepted_tokens holds {engine.numel()} counts for "
+                             f"{reqs} requests")
+        engine = engine[:reqs].clamp_min(1)
+    width = min(table.shape[1], positions)
+    prev = getattr(m, "block_idx_last_scheduled_token_prev_step", None)
+    sched = getattr(m, "block_idx_last_scheduled_token", None)
+    if prev is not None and sched is not None:
+        # prefix caching ("all" mode): the live window moves along the table
+        in_slots = _pick_columns(table, prev[:reqs], width)
+        out_slots = _pick_columns(table, sched[:reqs], width)
     else:
-        if starts.numel() < num_reqs + 1:
-            raise ValueError(f"query_start_loc_d is too short: shape={tuple(starts.shape)}, "
-                             f"num_decodes={num_reqs}")
-        starts = starts[: num_reqs + 1]
-    if accepted is False:  # the caller needs the slots only
-        accepted = None
-    elif accepted is None:
-        accepted = _accepted_tokens(m, num_reqs, slots.device)
-    else:
-        accepted = accepted[:num_reqs]
-    slots = slots[:num_reqs]
-    previous = getattr(m, "block_idx_last_scheduled_token_prev_step", None)
-    scheduled = getattr(m, "block_idx_last_scheduled_token", None)
-    ins = outs = slots
-    if previous is not None and scheduled is not None:
-        width = slots.shape[1] if max_positions is None else min(slots.shape[1], max_positions)
-        off = torch.arange(width, device=slots.device, dtype=torch.long)
-        ins = slots.gather(1, previous[:num_reqs, None].long() + off)
-        outs = slots.gather(1, scheduled[:num_reqs, None].long() + off)
-    elif max_positions is not None:
-        ins = outs = slots[:, :max_positions]
-    return ins, outs, starts, accepted
+        in_slots = out_slots = table[:, :width]
+    conv_table = _profiling_table(table, num_blocks)
+    comp = getattr(m, "block_idx_last_computed_token", None)
+    conv_in = (_pick_columns(conv_table, comp[:reqs], 1)[:, 0] if comp is not None
+               else conv_table[:, 0])
+    conv_out = (_pick_columns(conv_table, sched[:reqs], 1)[:, 0] if sched is not None
+                else conv_table[:, 0])
+    return DecodePlan(reqs, conv_table, _profiling_table(in_slots, num_blocks),
+                      _profiling_table(out_slots, num_blocks), starts, conv_in, conv_out, engine)
 
 
 class HyenaMixerBase(nn.Module):
@@ -226,7 +267,7 @@ class HyenaMixerBase(nn.Module):
         else:
             self.in_proj = Bf16Linear(h, 3 * hl, bias=False, device=device)
         self.out_proj = Bf16Linear(hl, h, bias=True, device=device)
-        self.out_proj.skip_bias = tp_size > 1
+        self.out_proj.skip_bias = tp_size > 1 and tp_rank != 0
         self.short_filter = nn.Parameter(torch.empty(3 * hl, 1, self.k_short, dtype=torch.bfloat16,
                                                      device=device), requires_grad=False)
         self.kv_cache = (torch.tensor([]), torch.tensor([]), torch.tensor([]))
@@ -311,64 +352,61 @@ class HyenaMixerBase(nn.Module):
         return lookup(self.prefix)
 
     # ---- position stamps (mixers.py:952-1074) ---------------------------------
+    # One fp32 per state block (S2's last column of channel 0) records how many
+    # tokens the block's snapshot represents; speculative rollback and the
+    # prefix-cache repair are decided from it on the device, in small kernels
+    # (csrc/spec.cu), so no step ever synchronises with the host.
     def _position_stamps(self):
         return self.kv_cache[2][:, 0, -1]
 
-    def _spec_accepted(self, m):
-        """Accepted tokens per request from the position stamps (mixers.py:962-984),
-        in one kernel (hyena_spec_accepted).  A mismatching stamp, where the
-        reference's device assert fires, is clamped and reported through the
-        kernel's error word instead."""
-        nd = int(m.num_decodes)
+    def _num_blocks(self):
+        return min(int(t.shape[0]) for t in self.kv_cache)
+
+    def _decode_plan(self, m):
+        return plan_decode(m, 1 + self.num_spec, self._num_blocks())
+
+    def _accepted_from_stamps(self, m, plan):
+        """Tokens accepted at the previous verify step, per request: the gap
+        between the request's computed-token count and the stamp of its first
+        block, clamped to [0, num_spec], plus one (hyena_spec_accepted; the
+        reference derives it at mixers.py:962-984 and asserts on a mismatch,
+        which here sets HYENA_FLAG_STAMP in the kernel's error word)."""
         computed = getattr(m, "num_computed_tokens_d", None)
         if computed is None:
-            raise RuntimeError("speculative Hyena decode needs num_computed_tokens_d "
-                               "(HyenaMamba2Backend metadata)")
-        slots = m.state_indices_tensor_d[:nd]
-        if slots.dim() == 1:
-            slots = slots[:, None]
-        slots = _cache_safe_state_indices(slots, self.kv_cache[2])
-        return ops.spec_accepted(slots, computed[:nd], self._position_stamps(), self.num_spec)
+            raise RuntimeError(f"{self.prefix}: speculative decode needs num_computed_tokens_d "
+                               "in the step metadata (the engine's Hyena metadata builder)")
+        return ops.spec_accepted(plan.table, computed[: plan.reqs], self._position_stamps(),
+                                 self.num_spec)
 
-    def _repair_resumed_prefill_state(self, m):
-        if not self.num_spec or not int(m.num_prefills):
-            return
-        computed = getattr(m, "computed_before_p", None)
-        src = getattr(m, "state_src_block_p", None)
-        has_init = getattr(m, "has_initial_states_p", None)
-        if computed is None or src is None or has_init is None:
-            return
+    def _repair_prefill_blocks(self, m):
+        """Prefix caching can hand a resumed prefill row a block whose snapshot
+        is not the one at its computed-token count (the reference documents the
+        case at mixers.py:1001-1037); hyena_state_repair copies the block of the
+        row's last computed token over it when that one carries the right stamp."""
         npf = int(m.num_prefills)
-        dst = m.state_indices_tensor_p[:npf].long()
-        src = src[:npf].long()
-        computed = computed[:npf].to(torch.float32)
-        stamps = self._position_stamps()
-        bad = (has_init[:npf].bool() & (stamps[dst] != computed) & (stamps[src] == computed)
-               & (src != 0) & (dst != 0))
-        take = torch.where(bad, src, dst)
-        for state in self.kv_cache:
-            state[dst] = state[take]
+        fields = [getattr(m, f, None) for f in ("computed_before_p", "state_src_block_p",
+                                                 "has_initial_states_p")]
+        if not self.num_spec or npf == 0 or any(f is None for f in fields):
+            return
+        computed, src, has_init = fields
+        ops.state_repair(m.state_indices_tensor_p[:npf], src, computed, has_init,
+                         self._position_stamps(), list(self.kv_cache))
 
-    def _resolve_accepted(self, m):
-        if self.num_spec and int(m.num_decodes) and self.is_speculative_decode(m):
-            return self._spec_accepted(m)
-        return None
-
-    def _record_stamps(self, m):
-        """Stamps of the slots written this step (mixers.py:1040-1074): verifier
-        slots in one kernel (hyena_spec_record), prefill blocks in torch."""
+    def _stamp_written_blocks(self, m, plan):
+        """After the step: every verifier slot written gets computed + p + 1
+        (hyena_spec_record) and every prefill block its sequence length
+        (hyena_spec_record_prefill), as mixers.py:1040-1074 requires."""
         if not self.num_spec:
             return
         stamps = self._position_stamps()
-        nd = int(m.num_decodes)
-        if nd and self.is_speculative_decode(m):
-            _, outs, starts, _ = _decode_tensors(m, int(m.num_decode_tokens), 1 + self.num_spec,
-                                                 accepted=False)
-            outs = _cache_safe_state_indices(outs, self.kv_cache[2])
-            ops.spec_record(outs, starts, m.num_computed_tokens_d[:nd], stamps)
-        npf = int(m.num_prefills)
+        if plan is not None and self.is_speculative_decode(m):
+            starts = plan.starts
+            if starts is None:
+                starts = torch.arange(plan.reqs + 1, device=plan.table.device, dtype=torch.int32)
+            ops.spec_record(plan.out_slots, starts, m.num_computed_tokens_d[: plan.reqs], stamps)
+        npf, nd = int(m.num_prefills), int(m.num_decodes)
         if npf:
-            stamps[m.state_indices_tensor_p[:npf].long()] = m.seq_lens[nd:nd + npf].to(stamps.dtype)
+            ops.spec_record_prefill(m.state_indices_tensor_p[:npf], m.seq_lens[nd:nd + npf], stamps)
 
     # ---- forward ----------------------------------------------------------------
     def _project(self, hidden_states, token_ids=None, pre_norm=None, residual=None):
@@ -414,31 +452,27 @@ class HyenaMixerBase(nn.Module):
             s0 = s0.transpose(-1, -2)
         return s0, self._inner_state_view()
 
-    def _run_core(self, z, m, accepted):
-        """g (T, H) = the mixer core on z (T, 3H); decode rows first, then prefill."""
+    def _run_core(self, z, m, accepted, plan=None):
+        """g (T, H) = the mixer core on z (T, 3H); decode rows first, then prefill.
+        plan: the step's DecodePlan (built here when the step has decode rows
+        and none is given); accepted: stamp-derived counts or None."""
         w = self._kernel_weights()
         nd, npt = int(m.num_decode_tokens), int(m.num_prefill_tokens)
         g = torch.empty(nd + npt, self.hidden, dtype=torch.bfloat16, device=z.device)
         conv, inner = self._states_for_kernels()
         if nd:
             if self.is_speculative_decode(m):
-                ins, outs, starts, acc = _decode_tensors(m, nd, 1 + self.num_spec, accepted)
-                ins = _cache_safe_state_indices(ins, inner)
-                outs = _cache_safe_state_indices(outs, inner)
-                slots = m.state_indices_tensor_d[: int(m.num_decodes)]
-                slots = slots[:, None] if slots.dim() == 1 else slots
-                slots = _cache_safe_state_indices(slots, conv)
-                sched = getattr(m, "block_idx_last_scheduled_token", None)
-                comp = getattr(m, "block_idx_last_computed_token", None)
-                nreq = slots.shape[0]
-                cin = slots.gather(1, comp[:nreq, None].long()).squeeze(1) if comp is not None else slots[:, 0]
-                cout = slots.gather(1, sched[:nreq, None].long()).squeeze(1) if sched is not None else slots[:, 0]
-                ops.decode(w, z[:nd], g[:nd], cin, cout, ins, outs, conv, inner,
-                           token_start=starts, accepted=acc, zero_null_rows=False,
-                           skip_null_writes=True)
+                plan = plan or self._decode_plan(m)
+                ops.decode(w, z[:nd], g[:nd], plan.conv_in, plan.conv_out, plan.in_slots,
+                           plan.out_slots, conv, inner, token_start=plan.starts,
+                           accepted=accepted if accepted is not None else plan.engine_accepted,
+                           zero_null_rows=False, skip_null_writes=True)
             else:
-                idx = self.decode_state_indices(m)[: int(m.num_decodes)]
-                ops.decode(w, z[:nd], g[:nd], idx, idx, idx[:, None], idx[:, None], conv, inner,
+                # one token per request, state read and written in place; rows
+                # on the null block are CUDA-graph padding (zero output, no write)
+                blk = self.decode_state_indices(m)[: int(m.num_decodes)]
+                col = blk.unsqueeze(1)
+                ops.decode(w, z[:nd], g[:nd], blk, blk, col, col, conv, inner,
                            zero_null_rows=True, skip_null_writes=True)
         if npt:
             ops.prefill(w, z[nd:nd + npt], g[nd:], m.query_start_loc_p,
@@ -446,15 +480,30 @@ class HyenaMixerBase(nn.Module):
                         m.state_indices_tensor_p[: int(m.num_prefills)], conv, inner)
         return g
 
-    def _out_proj(self, g, async_reduce=False, finish=None):
-        out, _ = self.out_proj(g)
+    def _out_proj(self, g, async_reduce=False, out=None):
+        """out_proj of g; with `out` (at least g's rows) the result is written
+        into its first rows.  Channel-sharded: the partial sums (rank 0's with the
+        bias from its GEMM epilogue) are all-reduced, left in flight when
+        async_reduce (PendingReduce)."""
+        y, _ = self.out_proj(g, out=None if out is None else out[: g.shape[0]])
+        full = y if out is None else out
         if self.tp_size > 1:
             if async_reduce:
-                return all_reduce_partial_async(out, self.out_proj.bias, self.tp_group, finish)
-            out = all_reduce_partial(out, self.out_proj.bias, self.tp_group)
-        if async_reduce:
-            return PendingReduce(out, None, None, finish)
-        return out
+                return all_reduce_partial_async(full, None, self.tp_group)
+            return all_reduce_partial(full, None, self.tp_group)
+        return PendingReduce(full, None, None) if async_reduce else full
+
+    def _output_buffer(self, hidden_states, rows):
+        """None when the mixer computes every row; else a (padded rows, H) tensor
+        whose rows past `rows` are zero.  Under CUDA graphs vLLM pads the token
+        count to a captured size and the decoder layer's residual add needs an
+        output of the padded length (mixers.py:1214-1228): the GEMM writes the
+        real rows into it directly, no copy."""
+        if rows == hidden_states.shape[0]:
+            return None
+        buf = torch.empty_like(hidden_states)
+        buf[rows:].zero_()
+        return buf
 
     def _forward_impl(self, hidden_states, token_ids=None, async_reduce=False, pre_norm=None,
                       residual=None):
@@ -464,17 +513,19 @@ class HyenaMixerBase(nn.Module):
         if m is None:
             out = self._profile_run(hidden_states, token_ids, pre_norm, residual)
             return PendingReduce(out, None, None) if async_reduce else out
-        self._repair_resumed_prefill_state(m)
-        accepted = self._resolve_accepted(m)  # before any state is written
+        self._repair_prefill_blocks(m)
         nd, npt = int(m.num_decode_tokens), int(m.num_prefill_tokens)
+        plan = self._decode_plan(m) if int(m.num_decodes) and self.is_speculative_decode(m) else None
+        # accepted counts come from the stamps before this layer writes any state
+        accepted = (self._accepted_from_stamps(m, plan)
+                    if plan is not None and self.num_spec else None)
         z = self._project(hidden_states[: nd + npt], token_ids, pre_norm,
                           None if residual is None else residual[: nd + npt])
-        g = self._run_core(z, m, accepted)
-        self._record_stamps(m)
-        finish = lambda out: self._unpad(out, hidden_states, nd + npt)  # noqa: E731
-        if async_reduce:
-            return self._out_proj(g, True, finish)
-        return finish(self._out_proj(g))
+        g = self._run_core(z, m, accepted, plan)
+        self._stamp_written_blocks(m, plan)
+        out = self._output_buffer(hidden_states, nd + npt)
+        res = self._out_proj(g, async_reduce, out)
+        return res
 
     def forward(self, hidden_states, token_ids=None, *, pre_norm=None, residual=None):
         """(T, H) bf16 -> (T, H) bf16 (mixers.py:823-829).
@@ -500,19 +551,13 @@ class HyenaMixerBase(nn.Module):
         return self._forward_impl(hidden_states, token_ids, async_reduce=True, pre_norm=pre_norm,
                                   residual=residual)
 
-    @staticmethod
-    def _unpad(out, hidden_states, n_actual):
-        if out.shape[0] == hidden_states.shape[0]:
-            return out
-        full = torch.zeros_like(hidden_states)
-        full[:n_actual] = out
-        return full
-
     def _profile_run(self, hidden_states, token_ids=None, pre_norm=None, residual=None):
-        """attn_metadata is None during a memory-profiling pass (mixers.py:1230-1235)."""
+        """vLLM's memory-profiling pass runs without metadata (mixers.py:1230-1235):
+        no state is touched; the triple product of the in_proj channels stands
+        in for the mixer so that both projections allocate what a step does."""
         z = self._project(hidden_states, token_ids, pre_norm, residual)
-        y = z[:, 0::3] * z[:, 1::3] * z[:, 2::3]
-        return self._out_proj(y.contiguous())
+        x2, x1, v = z.unflatten(-1, (self.hidden, 3)).unbind(-1)
+        return self._out_proj((x2 * x1 * v).contiguous())
 
     # ---- weights ------------------------------------------------------------------
     def load_full_weights(self, tensors: dict):

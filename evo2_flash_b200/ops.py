@@ -330,6 +330,24 @@ def gemm_e4m3(a, b, scale_a, scale_b, out=None):
     return out
 
 
+def gemm_wait_timeouts(reset: bool = False) -> int:
+    """Expired shared-memory barrier waits in the GEMMs on the current device
+    since the last reset (hyena_gemm_wait_timeouts; synchronous).  Non-zero
+    means some GEMM output was written from an incomplete tile."""
+    n = C.c_int32(0)
+    _lib.check(_lib.load().hyena_gemm_wait_timeouts(C.byref(n), int(bool(reset))),
+               "hyena_gemm_wait_timeouts")
+    return int(n.value)
+
+
+def check_gemm_waits() -> None:
+    """Raises RuntimeError when any GEMM wait expired on the current device."""
+    n = gemm_wait_timeouts()
+    if n:
+        raise RuntimeError(f"{n} GEMM shared-memory barrier wait(s) expired: "
+                           "GEMM outputs of this process are unreliable")
+
+
 def set_gemm_max_ctas(n: int) -> None:
     """Caps the CTAs of the large-M GEMMs (0: one per SM) so that collectives
     running on another stream find free SMs (hyena_set_gemm_max_ctas)."""
@@ -372,6 +390,59 @@ def spec_record(out_slots, starts, computed, stamps, error_flags=None):
     _lib.check(lib.hyena_spec_record(slots.data_ptr(), slots.stride(0), slots.stride(1), R, q,
                                      st.data_ptr(), comp.data_ptr(), base, stride, stamps.shape[0],
                                      _ptr(error_flags), _stream()), "hyena_spec_record")
+
+
+def spec_record_prefill(blocks, seq_lens, stamps, error_flags=None):
+    """stamp(blocks[j]) = seq_lens[j] (hyena_spec_record_prefill;
+    mixers.py:1070-1074).  blocks (n,) int (any stride), seq_lens (n,) int."""
+    n = blocks.shape[0]
+    if n == 0:
+        return
+    b = _i32(blocks, "blocks")
+    lens = _i32(seq_lens[:n].contiguous(), "seq_lens")
+    base, stride = _stamp_view(stamps)
+    _lib.check(_lib.load().hyena_spec_record_prefill(
+        b.data_ptr(), b.stride(0), n, lens.data_ptr(), base, stride, stamps.shape[0],
+        _ptr(error_flags), _stream()), "hyena_spec_record_prefill")
+
+
+def _block_slice(t):
+    """A StateBlock over a paged (blocks, ...) tensor whose blocks are contiguous."""
+    from ._lib import StateBlock
+
+    inner = t[0] if t.shape[0] else t
+    _require(inner.is_contiguous(), "state blocks must be contiguous within a block")
+    sb = StateBlock()
+    sb.data = t.data_ptr()
+    sb.block_stride_bytes = t.stride(0) * t.element_size()
+    sb.block_bytes = inner.numel() * t.element_size()
+    return sb
+
+
+def state_repair(dst_blocks, src_blocks, computed, has_init, stamps, states, error_flags=None):
+    """Prefix-caching repair of resumed prefill rows (hyena_state_repair;
+    mixers.py:1001-1037): where a row's destination block is not stamped with
+    its computed-token count but its source block is, the source block's whole
+    state (every tensor of `states`, each (blocks, ...)) is copied over the
+    destination.  Returns the (n,) int32 decision (source block or -1)."""
+    from ._lib import StateBlock
+
+    n = dst_blocks.shape[0]
+    take = torch.empty(max(n, 1), dtype=torch.int32, device=stamps.device)
+    if n == 0:
+        return take[:0]
+    dst = _i32(dst_blocks, "dst_blocks")
+    src = _i32(src_blocks[:n].contiguous(), "src_blocks")
+    comp = _i32(computed[:n].contiguous(), "computed")
+    init = has_init[:n]
+    init = (init if init.dtype == torch.bool else init != 0).contiguous().view(torch.uint8)
+    arr = (StateBlock * len(states))(*[_block_slice(t) for t in states])
+    base, stride = _stamp_view(stamps)
+    _lib.check(_lib.load().hyena_state_repair(
+        n, dst.data_ptr(), dst.stride(0), src.data_ptr(), comp.data_ptr(), init.data_ptr(), base,
+        stride, stamps.shape[0], arr, len(states), take.data_ptr(), _ptr(error_flags), _stream()),
+        "hyena_state_repair")
+    return take[:n]
 
 
 def set_launch_chaining(enable: bool) -> None:

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define HYENA_ABI_VERSION 5
+#define HYENA_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define HYENA_API __attribute__((visibility("default")))
@@ -118,8 +118,11 @@ HYENA_API int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_arg
  * 32 MiB array inside this library, present on every GPU that loads it until the
  * process exits.  LI prefills needing more (beyond ~32K packed tokens at
  * H = 4096) fail with HYENA_ERR_INVALID.  The first call on a device looks up
- * the array's device address; make it before any stream capture.  All calls
- * share the array: calls whose kernels overlap on the GPU race on it. */
+ * the array's device address; make it before any stream capture.  That
+ * address is cached per device for the process lifetime and belongs to the
+ * device's primary context: do not use this entry point after a
+ * cudaDeviceReset or from a non-primary context.  All calls share the array:
+ * calls whose kernels overlap on the GPU race on it. */
 HYENA_API int hyena_prefill_noalloc(const hyena_layer_params* p, const hyena_prefill_args* a,
                                     void* stream);
 
@@ -255,6 +258,51 @@ HYENA_API int hyena_spec_record(const int32_t* out_slots, int64_t s0, int64_t s1
                                 int32_t q, const int32_t* starts, const int32_t* computed,
                                 float* stamps, int64_t stamp_stride, int32_t num_blocks,
                                 int32_t* error_flags, void* stream);
+
+/* Every shared-memory barrier wait inside the GEMMs is bounded (4 s); a wait
+ * that expires is counted in a per-device counter and the kernel finishes
+ * without its tile being complete, so its output must not be trusted.  This
+ * copies the current device's counter into *count (a synchronous read: call it
+ * between steps, never during stream capture) and zeroes it when reset != 0.
+ * A non-zero count is the GEMMs' error report.  No counterpart in the reference
+ * (its GEMMs are library calls). */
+HYENA_API int hyena_gemm_wait_timeouts(int32_t* count, int32_t reset);
+
+/* Prefill stamps, replacing the prefill half of _record_stamps
+ * (mixers.py:1070-1074): stamp(blocks[j * block_stride]) = seq_lens[j] for
+ * j < n.  A block outside [0, num_blocks) sets HYENA_FLAG_BLOCK_RANGE. */
+HYENA_API int hyena_spec_record_prefill(const int32_t* blocks, int64_t block_stride, int32_t n,
+                                        const int32_t* seq_lens, float* stamps,
+                                        int64_t stamp_stride, int32_t num_blocks,
+                                        int32_t* error_flags, void* stream);
+
+/* One paged state slice for whole-block copies: block b occupies block_bytes
+ * contiguous bytes at data + b * block_stride_bytes (16-byte aligned, sizes in
+ * whole 16-byte words).  data == NULL: slice absent. */
+typedef struct hyena_state_block {
+  void* data;
+  int64_t block_stride_bytes;
+  int64_t block_bytes;
+} hyena_state_block;
+
+/* Prefix-caching repair of resumed prefill rows, replacing
+ * _repair_resumed_prefill_state (mixers.py:1001-1037).  For prefill row j
+ * (dst = dst_blocks[j * dst_stride], src = src_blocks[j], n = computed[j]):
+ * when has_init[j] != 0, neither block is the null block 0, stamp(dst) != n
+ * and stamp(src) == n, the whole state of block src (every slice given) is
+ * copied over block dst.  All decisions are taken from the stamps as they are
+ * before any copy (first kernel, into the caller's take[num_rows] int32
+ * buffer: source block or -1), then the copies run (second kernel).  Rows
+ * whose blocks lie outside [0, num_blocks) set HYENA_FLAG_BLOCK_RANGE and are
+ * not copied.  Distinct rows are assumed to name distinct destination blocks,
+ * none of which is another repaired row's source (live requests never share
+ * a block). */
+HYENA_API int hyena_state_repair(int32_t num_rows, const int32_t* dst_blocks, int64_t dst_stride,
+                                 const int32_t* src_blocks, const int32_t* computed,
+                                 const uint8_t* has_init, const float* stamps,
+                                 int64_t stamp_stride, int32_t num_blocks,
+                                 const hyena_state_block* slices, int32_t num_slices,
+                                 int32_t* take, int32_t* error_flags, void* stream);
 
 /* Caps the CTAs of the persistent (large-M) GEMMs at n (n <= 0: one per SM,
  * the default).  Process-wide.  A caller that overlaps GEMMs with collectives

@@ -293,4 +293,8 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # The reference checkout to run: first argument, else $EVO2_REFERENCE_ROOT.
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVO2_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <evo2_flash checkout> (or set EVO2_REFERENCE_ROOT)")
+    main(root)

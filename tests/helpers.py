@@ -24,6 +24,28 @@ def max_rel_err(a, b):
     return num / den
 
 
+def max_slice_rel_err(a, b, floor=1e-3):
+    """The larger of the row- and the column-normalised errors of 2-D outputs:
+    for every row (token) and every column (channel), max |a - b| over the
+    slice / max |b| over the slice.  Unlike max_rel_err, a wrong small-magnitude
+    token or channel cannot hide behind the largest value of the tensor.  A
+    slice whose max |b| is below `floor` x the global max |b| (an all-zero row,
+    say) is measured against that floor instead."""
+    a = a.float().reshape(a.shape[0], -1)
+    b = b.float().reshape(b.shape[0], -1)
+    diff = (a - b).abs()
+    mag = b.abs()
+    top = mag.max().item()
+    if top == 0.0:
+        return diff.max().item()
+    lo = floor * top
+    worst = 0.0
+    for dim in (1, 0):
+        den = mag.amax(dim).clamp_min(lo)
+        worst = max(worst, (diff.amax(dim) / den).max().item())
+    return worst
+
+
 def load_fixture(name):
     return torch.load(GOLDEN / f"{name}.pt", weights_only=False)
 

@@ -478,6 +478,22 @@ def test_small_m_gemm_cluster_split_k_is_deterministic(fp8, M):
     assert torch.equal(first, second)
 
 
+def test_gemm_barrier_waits_never_expired():
+    """The GEMMs bound every shared-memory barrier wait and count expiries in a
+    device counter; after every GEMM above (and one more of each kind here) the
+    counter, read back through hyena_gemm_wait_timeouts, is zero."""
+    from evo2_flash_b200 import ops
+
+    a = torch.randn(512, 1024, device=DEV).to(torch.bfloat16)
+    b = torch.randn(768, 1024, device=DEV).to(torch.bfloat16)
+    ops.gemm_bf16(a, b)
+    sc = torch.ones(1, device=DEV)
+    ops.gemm_e4m3(a.to(torch.float8_e4m3fn), b.to(torch.float8_e4m3fn), sc, sc)
+    torch.cuda.synchronize()
+    assert ops.gemm_wait_timeouts() == 0
+    ops.check_gemm_waits()
+
+
 def test_spec_bookkeeping_matches_the_stamp_rules():
     """hyena_spec_accepted / hyena_spec_record against the reference's torch
     rules (mixers.py:962-984, 1040-1062) on random stamps: accepted = clamp(
@@ -520,3 +536,49 @@ def test_spec_bookkeeping_matches_the_stamp_rules():
     torch.cuda.synchronize()
     got = ds2[:, 0, 16].cpu()
     assert torch.equal(got[1:], ref[1:])
+
+
+def test_state_repair_copies_stale_prefill_blocks():
+    """hyena_state_repair against the rule of mixers.py:1001-1037, restated on
+    the host: a resumed prefill row whose block is not stamped with its
+    computed-token count takes every state slice of its source block when
+    that one is; fresh rows, null blocks and consistent rows are untouched.
+    hyena_spec_record_prefill then stamps the prefill blocks."""
+    from evo2_flash_b200 import ops
+
+    g = torch.Generator().manual_seed(93)
+    nb, H, W0 = 24, 128, 5
+    states = [torch.randn(nb, W0, 3 * H, generator=g).to(torch.bfloat16),
+              torch.randn(nb, 127, H, generator=g), torch.randn(nb, H, 17, generator=g)]
+    states[2][:, 0, 16] = torch.randint(0, 50, (nb,), generator=g).float()
+    stamps = states[2][:, 0, 16]
+    dst = torch.tensor([3, 4, 5, 6, 7, 0, 8], dtype=torch.int32)
+    src = torch.tensor([10, 11, 12, 0, 13, 14, 15], dtype=torch.int32)
+    init = torch.tensor([True, True, False, True, True, True, True])
+    computed = stamps[src.long()].int().clone()
+    computed[1] = int(stamps[11]) + 1          # source stamp wrong: no copy
+    stamps[8] = float(computed[6])             # destination already right: no copy
+    want = [s.clone() for s in states]
+    bad = (init & (stamps[dst.long()] != computed.float()) & (stamps[src.long()] == computed.float())
+           & (src != 0) & (dst != 0))
+    for j in range(len(dst)):
+        if bad[j]:
+            for w in want:
+                w[dst[j]] = w[src[j]]
+    assert bad.tolist() == [True, False, False, False, True, False, False]
+    ds = [s.to(DEV) for s in states]
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    take = ops.state_repair(dst.to(DEV), src.to(DEV), computed.to(DEV), init.to(DEV),
+                            ds[2][:, 0, 16], ds, error_flags=flags)
+    torch.cuda.synchronize()
+    assert take.cpu().tolist() == [10, -1, -1, -1, 13, -1, -1]
+    for a, b in zip(ds, want):
+        assert torch.equal(a.cpu(), b)
+    lens = torch.tensor([60, 61, 62, 63, 64, 65, 66], dtype=torch.int32)
+    ops.spec_record_prefill(dst.to(DEV), lens.to(DEV), ds[2][:, 0, 16], error_flags=flags)
+    torch.cuda.synchronize()
+    got = ds[2][:, 0, 16].cpu()
+    for j in range(len(dst)):
+        if int(dst[j]):
+            assert got[int(dst[j])] == float(lens[j])
+    assert int(flags.item()) == 0
