@@ -215,7 +215,12 @@ class OracleMixer(torch.nn.Module):
                        torch.zeros(num_blocks, 127, H), torch.zeros(num_blocks, H, 16)]
 
     def forward(self, x, token_ids=None):
+        """Runs on the CPU whatever device the model is on; the result returns
+        to x's device (so the rest of the reference arm can stay on the GPU)."""
         from evo2_flash_b200.forward_context import get_forward_metadata
         from oracle.hyena_oracle import mixer_forward
 
-        return mixer_forward(x, self.p, get_forward_metadata(), self.states)
+        meta = get_forward_metadata()
+        meta = SimpleNamespace(**{k: (v.cpu() if isinstance(v, torch.Tensor) else v)
+                                  for k, v in vars(meta).items()})
+        return mixer_forward(x.cpu(), self.p, meta, self.states).to(x.device)
