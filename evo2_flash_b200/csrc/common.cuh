@@ -334,13 +334,23 @@ __device__ __forceinline__ bf162 bf162_from_f2(f2 v) {
 }
 
 // short_tap on a channel pair: products rounded to bf16 (bf16x2 multiply),
-// summed oldest first in fp32, result rounded to bf16.
+// summed oldest first in fp32 from a +0 accumulator, result rounded to bf16.
+// The sums use the mixed-precision add (a bf16 operand added to an fp32 one,
+// one fp32 rounding), so the bf16 products need no unpacking into fp32.
 __device__ __forceinline__ bf162 short_tap2(bf162 c0, bf162 c1, bf162 x, bf162 w0, bf162 w1,
                                             bf162 w2) {
-  const f2 p0 = f2_from_bf162(__hmul2(c0, w0));
-  const f2 p1 = f2_from_bf162(__hmul2(c1, w1));
-  const f2 p2 = f2_from_bf162(__hmul2(x, w2));
-  return bf162_from_f2(f2_add(f2_add(p0, p1), p2));
+  const uint32_t p0 = as_u32(__hmul2(c0, w0));
+  const uint32_t p1 = as_u32(__hmul2(c1, w1));
+  const uint32_t p2 = as_u32(__hmul2(x, w2));
+  float lo, hi;
+  asm("{\n\t.reg .b16 a0, a1, b0, b1, e0, e1;\n\t"
+      "mov.b32 {a0, a1}, %2;\n\tmov.b32 {b0, b1}, %3;\n\tmov.b32 {e0, e1}, %4;\n\t"
+      "add.rn.f32.bf16 %0, a0, 0f00000000;\n\tadd.rn.f32.bf16 %1, a1, 0f00000000;\n\t"
+      "add.rn.f32.bf16 %0, b0, %0;\n\tadd.rn.f32.bf16 %1, b1, %1;\n\t"
+      "add.rn.f32.bf16 %0, e0, %0;\n\tadd.rn.f32.bf16 %1, e1, %1;\n\t}"
+      : "=&f"(lo), "=&f"(hi)
+      : "r"(p0), "r"(p1), "r"(p2));
+  return __floats2bfloat162_rn(lo, hi);
 }
 
 // Largest j with qsl[j] <= row, for a non-decreasing qsl[0..n].

@@ -10,44 +10,118 @@
 // launch writes each segment's final windows (triton_prefill.py:433-459), so no
 // CTA can read a window another CTA already overwrote.
 //
-// Layout: a CTA owns 64 channels (192 z columns) and a contiguous range of packed
-// rows, and slides along time: u values live in a shared-memory ring indexed by
-// row, so the inner FIR's (K-1)-row halo is recomputed only once per CTA range
-// and at segment starts, not per tile.  Every z row is read once from HBM with
-// 16-byte vector loads; g is written once.
+// Layout: a CTA owns 16 channels (48 z columns) and a contiguous range of packed
+// rows, and slides along time in tiles of 256 rows:
+//   gate phase   z tile (cp.async, 3 stages) -> K=3 filter, x1*v on CUDA cores;
+//                u goes to a per-channel, time-major bf16 buffer in shared memory,
+//                x2 stays in registers;
+//   tap phase    the inner FIR as a banded Toeplitz product on the tensor cores
+//                (mma.sync m16n8k16, bf16 x bf16 -> fp32): per channel,
+//                Y(i, j) = y[t0 + 32 j + i] = sum_d W(i, d) U(d, j) with
+//                W(i, d) = w[d - i + K - 1] (the taps, zero outside [0, K)) and
+//                U(d, j) = u[t0 + 32 j + d].  W is fixed per channel and lives in
+//                registers as A fragments; the second 16-row M tile (i + 16) is
+//                the first one shifted by one k-step, so it reuses the same
+//                fragments.  U fragments come from that buffer with ldmatrix;
+//                results go back through stmatrix.trans into a per-channel,
+//                time-major y tile;
+//   store phase  + D*u, * x2, bf16 rounding as torch does, coalesced rows of g.
+// bf16 x bf16 products are exact in fp32, so the tensor-core form differs from
+// the reference's oldest-first fp32 sum only in the order of the additions.
+// The inner FIR's (K-1)-row halo is recomputed once per CTA range and at segment
+// starts.  Every z row is read once from HBM; g is written once.
+//
+// Shared-memory layouts avoid bank conflicts for every access pattern used:
+// per channel, u (halo + tile) and the y tile are stored as lines of 32 rows
+// with an 80-byte pitch (five 16-byte chunks, one of them padding) and an odd
+// per-channel chunk stride, so the eight row addresses of an ldmatrix /
+// stmatrix phase (rows 32 apart: chunks 5 apart) and the chunk pairs of the
+// gate and store phases fall on eight different bank groups, and every
+// ldmatrix address is a per-lane base plus a compile-time offset.  After each
+// tile its last HALO rows of u move to the front as the next tile's history.
+// z rows carry an 8-word gap after every 8 rows so that the four row groups of
+// a warp read disjoint banks.
 #include "common.cuh"
 
 namespace hb {
 
-constexpr int FIR_CG = 32;       // channels per CTA (two CTAs share an SM)
+constexpr int FIR_CG = 16;       // channels per CTA
 constexpr int FIR_PAIRS = FIR_CG / 2;
-constexpr int FIR_BT = 128;      // rows per tile
+constexpr int FIR_BT = 256;      // rows per tile
 constexpr int FIR_THREADS = 256;
-constexpr int FIR_RPT = 8;       // rows per thread in the gate and tap phases
-constexpr int FIR_RING = 256;    // u ring rows (power of two >= K-1 + FIR_BT)
-constexpr int FIR_WORDS = 3 * FIR_PAIRS;  // bf16x2 words of z per row per CTA
-constexpr int MAX_CONV_COLS = 8; // S0 window columns supported (K_short-1 + num_spec)
+constexpr int FIR_WARPS = FIR_THREADS / 32;
+constexpr int FIR_RPT = 8;       // rows per thread in the gate and store phases
+constexpr int FIR_WORDS = 3 * FIR_PAIRS;                       // bf16x2 z words per row
+constexpr int FIR_ZT_WORDS = FIR_WORDS * FIR_BT + 8 * (FIR_BT / 8);  // one z tile
+constexpr int FIR_YS_CH = (FIR_BT / 32) * 5 + 1;  // y tile chunks per channel (odd stride)
+constexpr int FIR_WOFF = 64;     // zero padding in front of the staged taps
+constexpr int FIR_STAGES = 3;    // z tiles in flight per CTA
 
-// z tiles in flight per CTA (one being consumed, the rest loading).  Three
-// stages for K = 7 measured no faster than two (the kernel is not bound by
-// bytes in flight), so both kernels use two.
+static_assert(FIR_PAIRS * (FIR_BT / FIR_RPT) == FIR_THREADS, "gate mapping");
+static_assert(2 * FIR_WARPS == FIR_CG, "two channels per warp in the tap phase");
+
+// u rows kept per channel: HALO rows of history (the tap phase reads from
+// d = -HALO) and the tile.
 template <int K>
-__host__ __device__ constexpr int fir_stages() {
-  return 2;
-}
+struct FirGeom {
+  static constexpr int HALO = 16 * ((K - 1 + 15) / 16);
+  static constexpr int LINES = (HALO + FIR_BT + 31) / 32;
+  static constexpr int UCH = (LINES * 5) | 1;  // 16-byte chunks per channel (odd stride)
+};
 
-// Thread (pair p = tid % 16, row group g = tid / 16) owns channels c0+2p, c0+2p+1
-// and tile rows 8g .. 8g+7 in both the gate and the tap phases (so the x2 it
-// gates with stays in its registers).
 template <int K>
 struct FirShared {
-  f2 ring[FIR_RING][FIR_PAIRS];                   // u by row (mod FIR_RING), fp32 pairs
-  uint32_t zt[fir_stages<K>()][FIR_BT][FIR_WORDS];  // z tiles (multi-buffered), bf16x2 words
-  f2 wsm[K][FIR_PAIRS];                           // inner taps as fp32 pairs, [k][pair]
+  uint32_t zt[FIR_STAGES][FIR_ZT_WORDS];  // z tiles, bf16x2 words
+  uint4 ub[FIR_CG * FirGeom<K>::UCH];     // u by (channel, row), bf16
+  // y tile by (channel, tile row); before the first tile it holds the taps,
+  // zero-padded, from which each warp builds its A fragments.
+  union {
+    uint4 ys[FIR_CG * FIR_YS_CH];
+    bf16 wpad[FIR_CG][K + 128];
+  };
   uint32_t zh[2][FIR_WORDS];             // z rows (r-2, r-1) before the tile
   bf162 sw[3][3][FIR_PAIRS];             // short taps [column x2/x1/v][tap][pair]
   bf162 dsm[FIR_PAIRS];
 };
+
+// Word offset of z tile row r (an 8-word gap after every 8 rows).
+__device__ __forceinline__ int zrow(int r) { return r * FIR_WORDS + 8 * (r >> 3); }
+
+// 16-byte chunk holding row t (t % 8 == 0: rows t..t+7) of one channel in a
+// line-padded per-channel array (32 rows per 80-byte line).
+__device__ __forceinline__ int line_chunk(int t) { return 5 * (t >> 5) + ((t & 31) >> 3); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(p))
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x4_trans(void* p, uint32_t r0, uint32_t r1, uint32_t r2,
+                                              uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(
+                   smem_u32(p)),
+               "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+               : "memory");
+}
+// d += a . b, m16n8k16, bf16 operands, fp32 accumulators.
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(bf16 lo, bf16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+__device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
+  return as_u32(__floats2bfloat162_rn(lo, hi));
+}
 
 struct SegCtx {
   int a, e;       // segment rows
@@ -79,18 +153,15 @@ __device__ __forceinline__ float z_at(const hyena_prefill_args& A, const SegCtx&
 }
 
 // u = bf16(x1 * v) of row t >= s.a for channel h, straight from global memory
-// (used for halos only).
-__device__ __forceinline__ float u_at(const hyena_prefill_args& A, const hyena_layer_params& P,
-                                      const SegCtx& s, long long t, int h) {
-  const bf16* sw = static_cast<const bf16*>(P.short_w);
-  float val[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int col = 3 * h + 1 + q;
-    val[q] = short_tap(z_at(A, s, t - 2, col), z_at(A, s, t - 1, col), z_at(A, s, t, col),
-                       ldbf(sw + col * 3), ldbf(sw + col * 3 + 1), ldbf(sw + col * 3 + 2));
-  }
-  return bf16r(val[0] * val[1]);
+// (used for halos only); w1 / w2: the x1 and v columns' short taps.
+__device__ __forceinline__ float u_at(const hyena_prefill_args& A, const SegCtx& s, long long t,
+                                      int h, const float (&w1)[3], const float (&w2)[3]) {
+  const int col = 3 * h + 1;
+  const float x1 = short_tap(z_at(A, s, t - 2, col), z_at(A, s, t - 1, col), z_at(A, s, t, col),
+                             w1[0], w1[1], w1[2]);
+  const float vv = short_tap(z_at(A, s, t - 2, col + 1), z_at(A, s, t - 1, col + 1),
+                             z_at(A, s, t, col + 1), w2[0], w2[1], w2[2]);
+  return bf16r(x1 * vv);
 }
 
 __device__ __forceinline__ uint32_t bf16_bits(float v) {
@@ -130,7 +201,7 @@ __device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefi
   constexpr int VPR = FIR_WORDS * 4 / 16;  // 16-byte vectors per row
   for (int i = threadIdx.x; i < t.n * VPR; i += FIR_THREADS) {
     const int row = i / VPR, v = i % VPR;
-    cp_async16(reinterpret_cast<uint4*>(&S.zt[buf][row][0]) + v,
+    cp_async16(&S.zt[buf][zrow(row) + 4 * v],
                reinterpret_cast<const uint4*>(z + (long long)(t.r + row) * A.ldz + 3 * c0) + v);
   }
   cp_async_commit();
@@ -141,16 +212,23 @@ __global__ void __launch_bounds__(FIR_THREADS, 2)
 fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int rows_per_cta) {
   pdl_entry();
   constexpr int HIST = K - 1;
-  static_assert(HIST + FIR_BT <= FIR_RING, "ring too small");
+  constexpr int KB = (HIST + 15) / 16;  // k-steps of U below d = 0
+  constexpr int NKS = KB + 2;           // k-steps of U: d in [DB0, 32)
+  constexpr int NA = NKS - 1;           // distinct W fragments
+  constexpr int DB0 = -16 * KB;
+  using G = FirGeom<K>;
+  static_assert(G::HALO == -DB0, "history rows");
+  static_assert(sizeof(bf16) * FIR_CG * (K + 128) <= sizeof(uint4) * FIR_CG * FIR_YS_CH,
+                "tap staging must fit in the y tile");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   FirShared<K>& S = *reinterpret_cast<FirShared<K>*>(smem_raw);
 
-  const int tid = threadIdx.x;
-  const int c0 = blockIdx.y * FIR_CG;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c0 = blockIdx.x * FIR_CG;
   const int nseg = A.num_segments;
   const int32_t* qsl = A.query_start_loc;
   const int T_end = min(A.T, __ldg(qsl + nseg));
-  const int r0 = blockIdx.x * rows_per_cta;
+  const int r0 = blockIdx.y * rows_per_cta;
   const int r1 = min(T_end, r0 + rows_per_cta);
   if (r0 >= r1) return;
 
@@ -160,23 +238,23 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float* s1 = static_cast<const float*>(A.inner_state.data);
 
-  constexpr int NST = fir_stages<K>();
   TileIt t = tile_at(A, r0, r1, find_segment(qsl, nseg, r0));
   int buf = 0;
   TileIt pf = t;  // the last tile put in flight
   prefetch_tile(S, A, pf, 0, c0);
 #pragma unroll
-  for (int s = 1; s < NST - 1; ++s) {
+  for (int s = 1; s < FIR_STAGES - 1; ++s) {
     pf = tile_at(A, pf.r + pf.n, r1, pf.j);
     prefetch_tile(S, A, pf, s, c0);
   }
 
-  for (int i = tid; i < K * FIR_PAIRS; i += FIR_THREADS) {
-    const int k = i / FIR_PAIRS, pp = i % FIR_PAIRS;
-    const long long h = c0 + 2 * pp;
-    S.wsm[k][pp] = f2_make(
-        __bfloat162float(iw[h * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]),
-        __bfloat162float(iw[(h + 1) * P.inner_w_stride_h + (long long)k * P.inner_w_stride_k]));
+  // ---- parameters: taps (zero-padded), short taps, D; the u buffer starts at zero
+  for (int i = tid; i < FIR_CG * (K + 128); i += FIR_THREADS) {
+    const int ch = i % FIR_CG, e = i / FIR_CG - FIR_WOFF;  // channel-fastest: coalesced taps
+    S.wpad[ch][e + FIR_WOFF] =
+        (e >= 0 && e < K)
+            ? iw[(long long)(c0 + ch) * P.inner_w_stride_h + (long long)e * P.inner_w_stride_k]
+            : __float2bfloat16_rn(0.0f);
   }
   for (int i = tid; i < 9 * FIR_PAIRS; i += FIR_THREADS) {
     const int col = i / (3 * FIR_PAIRS), tap = (i / FIR_PAIRS) % 3, pp = i % FIR_PAIRS;
@@ -187,17 +265,42 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   if (tid < FIR_PAIRS)
     S.dsm[tid] = Dg ? __halves2bfloat162(Dg[c0 + 2 * tid], Dg[c0 + 2 * tid + 1])
                     : __floats2bfloat162_rn(0.f, 0.f);
+  for (int i = tid; i < FIR_CG * G::UCH; i += FIR_THREADS) S.ub[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
 
-  const int pp = tid % FIR_PAIRS;  // channel pair
-  const int rg = tid / FIR_PAIRS;  // row group 0..15 (FIR_BT / FIR_RPT)
-  float* ring_f = reinterpret_cast<float*>(&S.ring[0][0]);
+  // ---- W fragments of this warp's two channels (A operand of m16n8k16):
+  // a0a1 (i = g, d0 + {0,1}), a2a3 (i = g + 8, d0 + {0,1}), a4a5 / a6a7 the same at d0 + 8,
+  // with d0 = DB0 + 16 ks + 2q.
+  uint32_t af[2][NA][4];
+  {
+    const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const bf16* wc = &S.wpad[2 * warp + cc][FIR_WOFF + K - 1];  // wc[d - i] = W(i, d)
+#pragma unroll
+      for (int ks = 0; ks < NA; ++ks) {
+        const int d0 = DB0 + 16 * ks + 2 * q;
+        af[cc][ks][0] = pack_bf16(wc[d0 - g], wc[d0 + 1 - g]);
+        af[cc][ks][1] = pack_bf16(wc[d0 - g - 8], wc[d0 + 1 - g - 8]);
+        af[cc][ks][2] = pack_bf16(wc[d0 + 8 - g], wc[d0 + 9 - g]);
+        af[cc][ks][3] = pack_bf16(wc[d0 + 8 - g - 8], wc[d0 + 9 - g - 8]);
+      }
+    }
+  }
+
+  // gate / store mapping: an 8-lane phase holds 4 channel pairs x 2 row groups
+  const int pp = (lane & 3) | ((lane >> 1) & 4);
+  const int rg = warp * 4 + (((lane >> 2) & 1) | ((lane >> 3) & 2));
+  const int g0 = rg * FIR_RPT;
+  bf16* ub_h = reinterpret_cast<bf16*>(S.ub);
   int cur_seg = -1;
 
   while (t.n > 0) {
     const TileIt nt = tile_at(A, t.r + t.n, r1, t.j);
-    // the tile NST-1 ahead goes into the buffer the previous tile has released
+    __syncthreads();  // the previous tile is finished: u buffer, y tile, z buffer, zh
+    // the tile FIR_STAGES-1 ahead goes into the buffer the previous tile released
     pf = tile_at(A, pf.r + pf.n, r1, pf.j);
-    prefetch_tile(S, A, pf, (buf + NST - 1) % NST, c0);
+    prefetch_tile(S, A, pf, (buf + FIR_STAGES - 1) % FIR_STAGES, c0);
 
     if (t.j != cur_seg) {
       // ---- new segment (or the CTA's first rows): history rows [r-HIST, r) and z rows r-2, r-1
@@ -208,13 +311,20 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         if (tid == 0) flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
         seg.init = false;
       }
-      __syncthreads();  // previous tile's readers of ring / zh are done
       for (int i = tid; i < HIST * FIR_CG; i += FIR_THREADS) {
         const int m = i / FIR_CG + 1, cc = i % FIR_CG;
         const long long tr = (long long)t.r - m;
         float val;
         if (tr >= seg.a) {
-          val = u_at(A, P, seg, tr, c0 + cc);
+          float w1[3], w2[3];  // the pair's short taps, from shared memory
+#pragma unroll
+          for (int k = 0; k < 3; ++k) {
+            const float2 a1 = __bfloat1622float2(S.sw[1][k][cc >> 1]);
+            const float2 a2 = __bfloat1622float2(S.sw[2][k][cc >> 1]);
+            w1[k] = (cc & 1) ? a1.y : a1.x;
+            w2[k] = (cc & 1) ? a2.y : a2.x;
+          }
+          val = u_at(A, seg, tr, c0 + cc, w1, w2);
         } else if (seg.init && seg.a - tr <= HIST) {
           const long long col = HIST - (seg.a - tr);
           val = s1[seg.blk * A.inner_state.block_stride + col * A.inner_state.col_stride +
@@ -222,7 +332,8 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         } else {
           val = 0.0f;
         }
-        ring_f[(int)(tr & (FIR_RING - 1)) * FIR_CG + cc] = val;
+        const int tr_rel = G::HALO - m;  // buffer row of input row t.r - m
+        ub_h[(cc * G::UCH + line_chunk(tr_rel & ~7)) * 8 + (tr_rel & 7)] = __float2bfloat16_rn(val);
       }
       for (int i = tid; i < 2 * FIR_WORDS; i += FIR_THREADS) {
         const int q = i / FIR_WORDS, wd = i % FIR_WORDS;
@@ -232,13 +343,13 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         S.zh[q][wd] = lo | (hi << 16);
       }
     }
-    cp_async_wait<NST - 1>();  // this tile's group (one group is committed per tile)
+    cp_async_wait<FIR_STAGES - 1>();  // this tile's group (one group is committed per tile)
     __syncthreads();
 
     const int n = t.n, r = t.r;
-    // ---- K=3 short filter on channel pairs, sliding over 8 consecutive rows
-    const int g0 = rg * FIR_RPT;
-    bf162 x2r[FIR_RPT];
+    const uint32_t* zt = S.zt[buf];
+    // ---- gate phase: K=3 short filter on a channel pair over 8 consecutive rows
+    uint32_t x2r[FIR_RPT];
     if (g0 < n) {
       bf162 w[3][3];
 #pragma unroll
@@ -247,88 +358,117 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         for (int k = 0; k < 3; ++k) w[c][k] = S.sw[c][k][pp];
       bf162 h2[3], h1[3];
       {
-        const uint32_t* a = g0 >= 2 ? &S.zt[buf][g0 - 2][3 * pp] : &S.zh[g0][3 * pp];
-        const uint32_t* b = g0 >= 1 ? &S.zt[buf][g0 - 1][3 * pp] : &S.zh[1][3 * pp];
+        const uint32_t* a = g0 >= 2 ? &zt[zrow(g0 - 2) + 3 * pp] : &S.zh[g0][3 * pp];
+        const uint32_t* b = g0 >= 1 ? &zt[zrow(g0 - 1) + 3 * pp] : &S.zh[1][3 * pp];
         split_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
         split_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
       }
+      uint32_t uu[FIR_RPT];
+      const uint32_t* zg = &zt[zrow(g0) + 3 * pp];  // rows g0.. of one 8-row group
 #pragma unroll
       for (int i = 0; i < FIR_RPT; ++i) {
-        const int row = g0 + i;
-        if (row < n) {
-          bf162 cur[3], o[3];
-          split_triples(S.zt[buf][row][3 * pp], S.zt[buf][row][3 * pp + 1],
-                        S.zt[buf][row][3 * pp + 2], cur[0], cur[1], cur[2]);
+        const uint32_t* zr = zg + i * FIR_WORDS;
+        bf162 cur[3], o[3];
+        split_triples(zr[0], zr[1], zr[2], cur[0], cur[1], cur[2]);
 #pragma unroll
-          for (int c = 0; c < 3; ++c) {
-            o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
-            h2[c] = h1[c];
-            h1[c] = cur[c];
-          }
-          S.ring[(r + row) & (FIR_RING - 1)][pp] = f2_from_bf162(__hmul2(o[1], o[2]));
-          x2r[i] = o[0];
+        for (int c = 0; c < 3; ++c) {
+          o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
+          h2[c] = h1[c];
+          h1[c] = cur[c];
         }
+        // rows past the tile read stale shared memory: their u must not reach the buffer
+        uu[i] = g0 + i < n ? as_u32(__hmul2(o[1], o[2])) : 0u;
+        x2r[i] = as_u32(o[0]);
+      }
+      // channel pairs by row -> 8 consecutive rows per channel
+      uint4 ua, ub;
+      ua.x = __byte_perm(uu[0], uu[1], 0x5410); ub.x = __byte_perm(uu[0], uu[1], 0x7632);
+      ua.y = __byte_perm(uu[2], uu[3], 0x5410); ub.y = __byte_perm(uu[2], uu[3], 0x7632);
+      ua.z = __byte_perm(uu[4], uu[5], 0x5410); ub.z = __byte_perm(uu[4], uu[5], 0x7632);
+      ua.w = __byte_perm(uu[6], uu[7], 0x5410); ub.w = __byte_perm(uu[6], uu[7], 0x7632);
+      S.ub[2 * pp * G::UCH + line_chunk(G::HALO + g0)] = ua;
+      S.ub[(2 * pp + 1) * G::UCH + line_chunk(G::HALO + g0)] = ub;
+    }
+    __syncthreads();
+
+    // ---- tap phase: per channel, Y (32 x 8) = W (32 x 16 NKS) . U (16 NKS x 8)
+    {
+      // ldmatrix rows: U(d, j) for j = lane & 7 at d = DB0 + 16 ks + 8 ((lane >> 3) & 1),
+      // buffer row HALO + 32 j + d = 32 j + 16 ks + 8 ((lane >> 3) & 1)
+      const int lbase = 5 * (lane & 7) + ((lane >> 3) & 1);
+      // stmatrix.trans rows: matrix k = (M tile m, half h), row q = column j of Y:
+      // tile rows 32 q + 16 m + 8 h
+      const int sk = lane >> 3, sq = lane & 7;
+      const int sbase = 5 * sq + 2 * (sk >> 1) + (sk & 1);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int ch = 2 * warp + cc;
+        float acc[2][4];
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[m][e] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          uint32_t b0, b1;
+          ldsm_x2(b0, b1, &S.ub[ch * G::UCH + lbase + 5 * (ks >> 1) + 2 * (ks & 1)]);
+          if (ks < NA) mma_bf16(acc[0], af[cc][ks], b0, b1);
+          if (ks >= 1) mma_bf16(acc[1], af[cc][ks - 1], b0, b1);
+        }
+        stsm_x4_trans(&S.ys[ch * FIR_YS_CH + sbase], pack_rn(acc[0][0], acc[0][1]),
+                      pack_rn(acc[0][2], acc[0][3]), pack_rn(acc[1][0], acc[1][1]),
+                      pack_rn(acc[1][2], acc[1][3]));
       }
     }
     __syncthreads();
 
-    // ---- z history for the next tile (reads zt/zh only; ring untouched)
+    // ---- store phase: g = bf16(x2 * bf16(y + bf16(D * u))) on channel pairs
+    if (g0 < n) {
+      const uint4 ya = S.ys[2 * pp * FIR_YS_CH + line_chunk(g0)];
+      const uint4 yb = S.ys[(2 * pp + 1) * FIR_YS_CH + line_chunk(g0)];
+      const uint32_t yaw[4] = {ya.x, ya.y, ya.z, ya.w}, ybw[4] = {yb.x, yb.y, yb.z, yb.w};
+      uint32_t uaw[4] = {0, 0, 0, 0}, ubw[4] = {0, 0, 0, 0};
+      const bool has_d = Dg != nullptr;
+      if (has_d) {
+        const uint4 ua = S.ub[2 * pp * G::UCH + line_chunk(G::HALO + g0)];
+        const uint4 ub = S.ub[(2 * pp + 1) * G::UCH + line_chunk(G::HALO + g0)];
+        uaw[0] = ua.x; uaw[1] = ua.y; uaw[2] = ua.z; uaw[3] = ua.w;
+        ubw[0] = ub.x; ubw[1] = ub.y; ubw[2] = ub.z; ubw[3] = ub.w;
+      }
+      const bf162 d2 = S.dsm[pp];
+      bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + g0) * A.ldo + c0) + pp;
+      const long long ld2 = A.ldo / 2;
+#pragma unroll
+      for (int i = 0; i < FIR_RPT; ++i) {
+        if (g0 + i < n) {
+          const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+          bf162 y = as_bf162(__byte_perm(yaw[i >> 1], ybw[i >> 1], sel));
+          if (has_d) y = __hadd2(y, __hmul2(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
+          outp[i * ld2] = __hmul2(as_bf162(x2r[i]), y);
+        }
+      }
+    }
+    // ---- z history for the next tile of this segment (z buffer and zh only)
     if (tid < FIR_WORDS) {
       uint32_t h0v, h1v;
       if (n >= 2) {
-        h0v = S.zt[buf][n - 2][tid];
-        h1v = S.zt[buf][n - 1][tid];
+        h0v = zt[zrow(n - 2) + tid];
+        h1v = zt[zrow(n - 1) + tid];
       } else {
         h0v = S.zh[1][tid];
-        h1v = S.zt[buf][0][tid];
+        h1v = zt[zrow(0) + tid];
       }
       S.zh[0][tid] = h0v;
       S.zh[1][tid] = h1v;
     }
-
-    // ---- inner FIR over the ring: thread = (channel pair, rows i0..i0+7)
-    const int i0 = rg * FIR_RPT;
-    if (i0 < n) {
-      f2 acc[FIR_RPT];
-#pragma unroll
-      for (int q = 0; q < FIR_RPT; ++q) acc[q] = 0ull;  // +0.0f in both lanes
-      const int base = r + i0 - HIST;  // may be negative: masked arithmetic wraps
-      f2 cur[8], nxt[8];
-#pragma unroll
-      for (int x = 0; x < 8; ++x) cur[x] = S.ring[(base + x) & (FIR_RING - 1)][pp];
-#pragma unroll
-      for (int kb = 0; kb < K; kb += 8) {
-#pragma unroll
-        for (int x = 0; x < 8; ++x)
-          if (kb + 8 + x < HIST + FIR_RPT) nxt[x] = S.ring[(base + kb + 8 + x) & (FIR_RING - 1)][pp];
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          if (kb + kk < K) {
-            const f2 wv = S.wsm[kb + kk][pp];
-#pragma unroll
-            for (int q = 0; q < FIR_RPT; ++q)
-              acc[q] = f2_fma(wv, (q + kk < 8) ? cur[q + kk] : nxt[q + kk - 8], acc[q]);
-          }
-        }
-#pragma unroll
-        for (int x = 0; x < 8; ++x) cur[x] = nxt[x];
-      }
-      const bool has_d = Dg != nullptr;
-      const bf162 d2 = S.dsm[pp];
-      bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + i0) * A.ldo + c0) + pp;
-      const long long ld2 = A.ldo / 2;
-#pragma unroll
-      for (int q = 0; q < FIR_RPT; ++q) {
-        if (i0 + q < n) {
-          bf162 y = bf162_from_f2(acc[q]);
-          if (has_d)
-            y = __hadd2(y, __hmul2(d2, bf162_from_f2(S.ring[(r + i0 + q) & (FIR_RING - 1)][pp])));
-          outp[q * ld2] = __hmul2(x2r[q], y);
-        }
-      }
+    // ---- the tile's last HALO rows of u become the next tile's history
+    // (read from rows the store phase does not touch; written over rows no
+    // one reads until the next tile's tap phase)
+    for (int i = tid; i < FIR_CG * (G::HALO / 8); i += FIR_THREADS) {
+      const int cc = i / (G::HALO / 8), c8 = 8 * (i % (G::HALO / 8));
+      S.ub[cc * G::UCH + line_chunk(c8)] = S.ub[cc * G::UCH + line_chunk(FIR_BT + c8)];
     }
-    __syncthreads();
-    buf = (buf + 1) % NST;
+    buf = (buf + 1) % FIR_STAGES;
     t = nt;
   }
 }
@@ -439,13 +579,16 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   const size_t smem = sizeof(FirShared<K>);
   if (!smem_attr<fir_prefill_kernel<K>>((int)smem))
     return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(fir_prefill) failed");
-  // Rows per CTA: long enough that the (K-1)-row halo is a small fraction,
-  // short enough to fill the 148 SMs several times over.
+  // Rows per CTA: a multiple of the tile, long enough that the (K-1)-row halo is
+  // a small fraction, short enough to fill the 148 SMs several times over.
   const int groups = P.H / FIR_CG;
   int rows = K > 16 ? 2048 : 1024;
   const long long want_ctas = 148LL * 8;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
-  dim3 grid((A.T + rows - 1) / rows, groups);
+  while ((A.T + rows - 1) / rows > 65535) rows *= 2;
+  // channel groups fastest: CTAs that run together read neighbouring 96-byte
+  // pieces of the same z rows
+  dim3 grid(groups, (A.T + rows - 1) / rows);
   launch_kernel(fir_prefill_kernel<K>, dim3(grid), dim3(FIR_THREADS), smem, st, 0u, P, A, rows);
   int rc = check_launch("fir_prefill_kernel");
   if (rc) return rc;
@@ -455,6 +598,7 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
 }
 
 int fir_prefill_launch(const hyena_layer_params& P, const hyena_prefill_args& A, cudaStream_t st) {
+  if (P.H % FIR_CG != 0) return fail(HYENA_ERR_INVALID, "FIR prefill needs H % 16 == 0");
   if (P.K == 128) return launch_fir<128>(P, A, st);
   if (P.K == 7) return launch_fir<7>(P, A, st);
   return fail(HYENA_ERR_UNSUPPORTED, "FIR prefill supports K = 7 or 128");

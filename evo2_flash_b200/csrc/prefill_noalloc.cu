@@ -2,7 +2,7 @@
 // allocate device memory.
 //
 // hyena_prefill needs a caller-provided workspace for the LI (HCL) kind: the
-// chunk table and the carried modal states of the chunked scan.  Some callers
+// range table and the carried modal states of the chunked scan.  Some callers
 // have no way to provide one: a host program in another language that reaches
 // this library only through the C ABI and has no CUDA allocator of its own, or
 // an engine that launches from inside CUDA-graph stream capture, where
@@ -13,8 +13,10 @@
 //
 // Limits and contract:
 //   * the scratch is NOALLOC_SCRATCH_BYTES (32 MiB) on every GPU that loads the
-//     library, held until the process exits; an LI prefill needing more (more
-//     than ~32K packed tokens at H = 4096) is rejected with HYENA_ERR_INVALID;
+//     library, held until the process exits.  The LI prefill needs one (H, 16)
+//     fp32 modal state per segment plus a few for splitting long segments
+//     (256 KiB each at H = 4096); a step needing more (beyond ~120 segments at
+//     H = 4096) is rejected with HYENA_ERR_INVALID;
 //   * the first call on a device looks the array's device address up (once per
 //     device, with that device current); make that first call before any
 //     stream capture.  The address is cached per device ordinal for the life of
@@ -22,7 +24,7 @@
 //     CUDA runtime uses): callers that make another context current, or reset
 //     the device (cudaDeviceReset), must not use this entry point afterwards;
 //   * every call shares the one array and leaves its contents behind: nothing in
-//     it needs to start at zero (the chunk table and every carried state are
+//     it needs to start at zero (the range table and every carried state are
 //     written before they are read), but two calls whose kernels overlap on the
 //     GPU (different streams, or different host threads) race on it.  Serialise
 //     them on one stream.

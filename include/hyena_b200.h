@@ -116,8 +116,10 @@ HYENA_API int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_arg
  * the reference (its Python path allocates through torch).  Same arguments and
  * result as hyena_prefill minus the workspace: the LI kind's scratch is a fixed
  * 32 MiB array inside this library, present on every GPU that loads it until the
- * process exits.  LI prefills needing more (beyond ~32K packed tokens at
- * H = 4096) fail with HYENA_ERR_INVALID.  The first call on a device looks up
+ * process exits.  The LI kind needs one (H, 16) fp32 modal state per
+ * segment, plus a few for splitting long segments (256 KiB each at H = 4096);
+ * steps needing more (beyond ~120 segments at H = 4096) fail with
+ * HYENA_ERR_INVALID.  The first call on a device looks up
  * the array's device address; make it before any stream capture.  That
  * address is cached per device for the process lifetime and belongs to the
  * device's primary context: do not use this entry point after a

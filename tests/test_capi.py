@@ -73,8 +73,15 @@ def test_workspace_size_only_for_li(lib):
     p.kind, p.H, p.K = 0, 4096, 128
     assert lib.hyena_prefill_workspace_size(C.byref(p), 65536, 8) == 0
     p.kind, p.K = 1, 16
+    state = 4096 * 16 * 4  # one (H, 16) fp32 modal state
     n = lib.hyena_prefill_workspace_size(C.byref(p), 65536, 8)
-    assert n >= (65536 // 256) * 4096 * 16 * 4
+    # a 256-byte range table, then one state per range: at least one range per
+    # segment plus one for a segment that is split
+    assert (n - 256) % state == 0 and (n - 256) // state >= 9
+    # ranges grow with the tokens only until the grid is full: 16x the tokens
+    # needs far less than 16x the scratch
+    n16 = lib.hyena_prefill_workspace_size(C.byref(p), 16 * 65536, 8)
+    assert n16 < 2 * n
 
 
 def test_gemms_need_no_workspace(lib):

@@ -73,7 +73,7 @@ def test_noalloc_prefill_matches_workspace_prefill_on_two_calls():
         assert rc == 0, msg
         assert max_rel_err(out, ref) < REL_TOL
         assert torch.equal(new_states[0], ref_states[0])
-        assert max_rel_err(new_states[2], ref_states[2]) < REL_TOL
+        assert torch.equal(new_states[2], ref_states[2])  # the same kernels run
 
 
 def test_noalloc_prefill_rejects_a_step_beyond_the_scratch():
@@ -84,7 +84,9 @@ def test_noalloc_prefill_rejects_a_step_beyond_the_scratch():
     p.kind, p.H, p.K = _lib.HYENA_KIND_IIR, 4096, 16
     p.short_w, p.log_poles, p.residues = 1, 1, 1  # rejected before any is read
     a = PrefillArgs()
-    a.T, a.num_segments = 1 << 20, 1
+    # one 256 KiB modal state per segment (H = 4096): 200 segments need ~50 MiB
+    a.T, a.num_segments = 1 << 20, 200
     lib = _lib.load()
+    assert lib.hyena_prefill_workspace_size(C.byref(p), a.T, a.num_segments) > 32 << 20
     assert lib.hyena_prefill_noalloc(C.byref(p), C.byref(a), None) == 1
     assert b"32 MiB" in lib.hyena_last_error()
