@@ -443,7 +443,9 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         if (g0 + i < n) {
           const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
           bf162 y = as_bf162(__byte_perm(yaw[i >> 1], ybw[i >> 1], sel));
-          if (has_d) y = __hadd2(y, __hmul2(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
+          // D*u is rounded to bf16 before the add, as torch does: the _rn
+          // multiply keeps the compiler from fusing the two into one bf16 FMA
+          if (has_d) y = __hadd2(y, __hmul2_rn(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
           outp[i * ld2] = __hmul2(as_bf162(x2r[i]), y);
         }
       }

@@ -180,12 +180,18 @@ __device__ __forceinline__ void hmma(float (&d)[4], const uint32_t (&a)[4], cons
 __device__ __forceinline__ uint32_t hpack(float lo, float hi) {
   return as_u32(__floats2bfloat162_rn(lo, hi));
 }
-// x = hi + lo with hi = bf16(x), lo = bf16(x - hi): bf16x2 words of two values.
-__device__ __forceinline__ void hsplit2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+// x = hi + mid + lo, each bf16, |x - hi - mid - lo| <= 2^-24 |x| (each
+// remainder is exact in fp32): bf16x2 words of two values.
+__device__ __forceinline__ void hsplit3(float x0, float x1, uint32_t& hi, uint32_t& mid,
+                                        uint32_t& lo) {
   const bf162 h = __floats2bfloat162_rn(x0, x1);
   const float2 hf = __bfloat1622float2(h);
+  const float r0 = x0 - hf.x, r1 = x1 - hf.y;
+  const bf162 m = __floats2bfloat162_rn(r0, r1);
+  const float2 mf = __bfloat1622float2(m);
   hi = as_u32(h);
-  lo = hpack(x0 - hf.x, x1 - hf.y);
+  mid = as_u32(m);
+  lo = hpack(r0 - mf.x, r1 - mf.y);
 }
 
 __device__ __forceinline__ uint32_t hbits(float v) {
@@ -297,10 +303,12 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
   __syncthreads();
 
   // ---- constant B fragments of this warp's channel (k16 x n8: b0 = (k = 2q, 2q+1; n = g),
-  // b1 = (k + 8; n = g)), each split into hi / lo bf16
+  // b1 = (k + 8; n = g)), each split into hi / mid / lo bf16 so that the products
+  // with the bf16 data carry fp32 accuracy
   const int ch = warp, g = lane >> 2, q = lane & 3;
   const int h = c0 + ch;
-  uint32_t Gh[2][2][2], Gl[2][2][2];  // [ks][n-tile]: G(tau = 16 ks + k, s = 8 n + g)
+  const float* lph = lpg + (long long)h * P.lp_stride_h;
+  uint32_t G3[3][2][2][2];  // [split][ks][n-tile][b]: G(tau = 16 ks + 8 b + 2q (+1), s = 8 n + g)
 #pragma unroll
   for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
@@ -308,11 +316,11 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
 #pragma unroll
       for (int b = 0; b < 2; ++b) {
         const int tau = 16 * ks + 8 * b + 2 * q;
-        const float lp = lpg[(long long)h * P.lp_stride_h + (long long)(8 * n + g) * P.lp_stride_s];
-        hsplit2(expf(lp * (float)(HCL_C - 1 - tau)), expf(lp * (float)(HCL_C - 2 - tau)),
-                Gh[ks][n][b], Gl[ks][n][b]);
+        const float lp = lph[(long long)(8 * n + g) * P.lp_stride_s];
+        hsplit3(expf(lp * (float)(HCL_C - 1 - tau)), expf(lp * (float)(HCL_C - 2 - tau)),
+                G3[0][ks][n][b], G3[1][ks][n][b], G3[2][ks][n][b]);
       }
-  uint32_t Vh[4][2], Vl[4][2];  // [n-tile]: V(s = k, i = 8 n + g) = R_s p_s^(i+1)
+  uint32_t V3[3][4][2];  // [split][n-tile][b]: V(s = 8 b + 2q (+1), i = 8 n + g) = R_s p_s^(i+1)
   {
     const float* rr = rsg + (long long)h * P.res_stride_h;
 #pragma unroll
@@ -321,24 +329,23 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
       for (int b = 0; b < 2; ++b) {
         const int s = 8 * b + 2 * q, i = 8 * n + g;
         const float v0 = rr[(long long)s * P.res_stride_s] *
-                         expf(lpg[(long long)h * P.lp_stride_h + (long long)s * P.lp_stride_s] * (float)(i + 1));
+                         expf(lph[(long long)s * P.lp_stride_s] * (float)(i + 1));
         const float v1 = rr[(long long)(s + 1) * P.res_stride_s] *
-                         expf(lpg[(long long)h * P.lp_stride_h + (long long)(s + 1) * P.lp_stride_s] * (float)(i + 1));
-        hsplit2(v0, v1, Vh[n][b], Vl[n][b]);
+                         expf(lph[(long long)(s + 1) * P.lp_stride_s] * (float)(i + 1));
+        hsplit3(v0, v1, V3[0][n][b], V3[1][n][b], V3[2][n][b]);
       }
   }
-  // T(tau, i) = h[i - tau] for i >= tau; nonzero (ks, n) blocks: ks 0 x n 0..3, ks 1 x n 2..3
-  uint32_t Th[6][2], Tl[6][2];
+  // T(tau, i) = h[i - tau] (i >= tau) depends on i - tau only: the fragment of
+  // (k-step ks, n-tile n) has b0 = word(8 n - 16 ks), b1 = word(8 n - 16 ks - 8)
+  // with word(x) = (h[x + g - 2q], h[x + g - 2q - 1]); five words cover the
+  // nonzero blocks (ks 0 x n 0..3, ks 1 x n 2..3): x = -8, 0, 8, 16, 24.
+  uint32_t T3[3][5];
 #pragma unroll
-  for (int f = 0; f < 6; ++f) {
-    const int ks = f < 4 ? 0 : 1, n = f < 4 ? f : f - 2;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      const int tau = 16 * ks + 8 * b + 2 * q, i = 8 * n + g;
-      const float t0 = i - tau >= 0 ? S.hf[ch][i - tau] : 0.0f;
-      const float t1 = i - tau - 1 >= 0 ? S.hf[ch][i - tau - 1] : 0.0f;
-      hsplit2(t0, t1, Th[f][b], Tl[f][b]);
-    }
+  for (int w = 0; w < 5; ++w) {
+    const int i0 = 8 * w - 8 + g - 2 * q;
+    const float t0 = i0 >= 0 ? S.hf[ch][i0] : 0.0f;
+    const float t1 = i0 - 1 >= 0 ? S.hf[ch][i0 - 1] : 0.0f;
+    hsplit3(t0, t1, T3[0][w], T3[1][w], T3[2][w]);
   }
 
   // ---- carried modal state: this lane's modes 2q, 2q+1, 8+2q, 9+2q
@@ -444,10 +451,9 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-        for (int nn = 0; nn < 2; ++nn) {
-          hmma(accA[nn], Ua[ks], Gh[ks][nn]);
-          hmma(accA[nn], Ua[ks], Gl[ks][nn]);
-        }
+        for (int nn = 0; nn < 2; ++nn)
+#pragma unroll
+          for (int sp = 2; sp >= 0; --sp) hmma(accA[nn], Ua[ks], G3[sp][ks][nn]);
       // carry over the chunks: inclusive Kogge-Stone scan of each row half over
       // the lanes g (stride 4), halves joined, then S_in(j) = P^j carry + E(j-1)
       float sin_lo[4], sin_hi[4];
@@ -474,28 +480,37 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
         carry[m] = fmaf(pws[HCL_NJ], carry[m], e15);
       }
       if (!AGG) {
-        // S_in as the A operand (16 chunks x 16 modes), hi / lo
-        uint32_t Sh[4], Sl[4];
-        hsplit2(sin_lo[0], sin_lo[1], Sh[0], Sl[0]);
-        hsplit2(sin_hi[0], sin_hi[1], Sh[1], Sl[1]);
-        hsplit2(sin_lo[2], sin_lo[3], Sh[2], Sl[2]);
-        hsplit2(sin_hi[2], sin_hi[3], Sh[3], Sl[3]);
+        // S_in as the A operand (16 chunks x 16 modes), hi / mid / lo
+        uint32_t S3[3][4];
+        hsplit3(sin_lo[0], sin_lo[1], S3[0][0], S3[1][0], S3[2][0]);
+        hsplit3(sin_hi[0], sin_hi[1], S3[0][1], S3[1][1], S3[2][1]);
+        hsplit3(sin_lo[2], sin_lo[3], S3[0][2], S3[1][2], S3[2][2]);
+        hsplit3(sin_hi[2], sin_hi[3], S3[0][3], S3[1][3], S3[2][3]);
         float accY[4][4];
 #pragma unroll
         for (int nn = 0; nn < 4; ++nn)
 #pragma unroll
           for (int e = 0; e < 4; ++e) accY[nn][e] = 0.0f;
+        // smaller terms first: the carried-state readout (every product of
+        // order >= 2^-16 of the leading one), then the intra-chunk Toeplitz
+#pragma unroll
+        for (int nn = 0; nn < 4; ++nn) {
+          hmma(accY[nn], S3[1], V3[1][nn]);
+          hmma(accY[nn], S3[2], V3[0][nn]);
+          hmma(accY[nn], S3[0], V3[2][nn]);
+          hmma(accY[nn], S3[1], V3[0][nn]);
+          hmma(accY[nn], S3[0], V3[1][nn]);
+          hmma(accY[nn], S3[0], V3[0][nn]);
+        }
 #pragma unroll
         for (int f = 0; f < 6; ++f) {
           const int ks = f < 4 ? 0 : 1, nn = f < 4 ? f : f - 2;
-          hmma(accY[nn], Ua[ks], Th[f]);
-          hmma(accY[nn], Ua[ks], Tl[f]);
-        }
+          const int w0 = nn - 2 * ks + 1;  // word index of x = 8 nn - 16 ks
 #pragma unroll
-        for (int nn = 0; nn < 4; ++nn) {
-          hmma(accY[nn], Sh, Vh[nn]);
-          hmma(accY[nn], Sh, Vl[nn]);
-          hmma(accY[nn], Sl, Vh[nn]);
+          for (int sp = 2; sp >= 0; --sp) {
+            const uint32_t tb[2] = {T3[sp][w0], T3[sp][w0 - 1]};
+            hmma(accY[nn], Ua[ks], tb);
+          }
         }
         // y (bf16) into the y tile: matrix k = (row half k & 1, n-tile 2x + (k >> 1))
         const int sk = lane >> 3, srr = lane & 7;
@@ -553,8 +568,10 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
           if (g0 + i < n) {
             const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
             bf162 y = as_bf162(__byte_perm(yaw[i >> 1], ybw[i >> 1], sel));
+            // D*u is rounded to bf16 before the add, as torch does: the _rn
+            // multiply keeps the compiler from fusing the two into one bf16 FMA
             if (has_d)
-              y = __hadd2(y, __hmul2(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
+              y = __hadd2(y, __hmul2_rn(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
             outp[i * ld2] = __hmul2(as_bf162(x2r[i]), y);
           }
         }
