@@ -529,10 +529,11 @@ H40 = 8192
 TP_TOKENS = 262144
 
 
-def run_tp40b(args, world, rank, device, dist_ok):
+def run_tp40b(args, world, rank, device, dist_ok, quiet=False):
     """40B-shape triple, channel-sharded over `world` ranks; chunked prefill with
     the row-parallel all-reduces in flight under the following chunks, then
-    batch-1 decode steps (eager, one all-reduce per layer)."""
+    batch-1 decode steps (eager, one all-reduce per layer).  Returns the JSON
+    line (printed by rank 0 unless `quiet`)."""
     import torch.distributed as dist
 
     from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer, set_forward_metadata
@@ -648,15 +649,17 @@ def run_tp40b(args, world, rank, device, dist_ok):
                    "steps": args.tp_decode_steps, "graph": False},
         "clocks": clk.summary(),
     }
-    if rank == 0:
+    if rank == 0 and not quiet:
         print(json.dumps(line))
+    return line
 
 
 
-def run_cp40b(args, world, rank, device, dist_ok):
+def run_cp40b(args, world, rank, device, dist_ok, quiet=False):
     """40B-shape triple, one 262144-token sequence split into `world`
     contiguous slices (context parallel); per layer the only collective is the
-    LI layer's all-gather of (H, 16) slice states."""
+    LI layer's all-gather of (H, 16) slice states.  Returns the JSON line
+    (printed by rank 0 unless `quiet`)."""
     from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer
     from evo2_flash_b200.context_parallel import cp_prefill, dist_gather, halo_rows
     from evo2_flash_b200.synthetic import mixer_tensors
@@ -729,8 +732,9 @@ def run_cp40b(args, world, rank, device, dist_ok):
         "tok_per_s_per_gpu": value / world,
         "clocks": clk.summary(),
     }
-    if rank == 0:
+    if rank == 0 and not quiet:
         print(json.dumps(line))
+    return line
 
 
 
@@ -800,7 +804,7 @@ def run_hcm256(args, device):
     print(json.dumps(line))
 
 
-def run_model7b(args, device):
+def run_model7b(args, device, quiet=False):
     """Config 4: the full random-init StripedHyena2 7B (32 blocks, attention at
     3/10/17/24/31, fp8 Hyena in_proj) scoring a bounded sample of the 64
     order-3-Markov ACGT sequences (lengths U[1k, 32k], seeded): prefill tok/s
@@ -833,7 +837,47 @@ def run_model7b(args, device):
                    "attention": "torch SDPA (outside the mixer path)"},
         "mean_nll": sum(nll) / len(nll),
     }
-    print(json.dumps(line))
+    if not quiet:
+        print(json.dumps(line))
+    return line
+
+
+def sharded_40b_record(args, world, rank, device, dist_ok):
+    """Config 5 inside the default run, so that every N of a scaling run records
+    the channel-sharded design: t1 = the unsharded 40B-shape triple on rank 0
+    alone (the same 32768-token chunks), then the tensor-parallel and the
+    context-parallel prefill over all `world` ranks, each with its parallel
+    efficiency t1 / (N t_N)."""
+    sub = SimpleNamespace(**vars(args))
+    sub.steps = 3
+    if world == 1:
+        tp = run_tp40b(sub, 1, 0, device, False, quiet=True)
+        t1 = tp["ms_per_step"]
+    else:
+        t1 = 0.0
+        if rank == 0:
+            t1 = run_tp40b(sub, 1, 0, device, False, quiet=True)["ms_per_step"]
+        torch.cuda.empty_cache()
+        torch.distributed.barrier()
+        tp = run_tp40b(sub, world, rank, device, True, quiet=True)
+    torch.cuda.empty_cache()
+    cp = run_cp40b(sub, world, rank, device, dist_ok, quiet=True)
+    torch.cuda.empty_cache()
+
+    def part(line):
+        t = line["ms_per_step"]
+        return {"ms_per_step": t, "tok_per_s": line["value"],
+                "tok_per_s_per_gpu": line["value"] / world,
+                "efficiency": t1 / (world * t), "parallelism": line["config"]["parallelism"],
+                "steps": sub.steps, "clocks": line.get("clocks")}
+
+    rec = {"workload": "config5: HCS+HCM+HCL triple at the 40B shape (H=8192, fp8 in_proj "
+                       "8192->24576), one 262144-token sequence",
+           "t1_ms": t1, "t1_source": "rank 0 alone, unsharded, same chunking as tp",
+           "tp": part(tp), "cp": part(cp)}
+    rec["tp"]["decode_ms_per_step"] = tp["decode"]["ms_per_step"]
+    rec["tp"]["decode_steps"] = tp["decode"]["steps"]
+    return rec
 
 
 # ---------------------------------------------------------------- main
@@ -843,10 +887,14 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--decode-steps", type=int, default=200)
+    ap.add_argument("--decode-steps", type=int, default=500)
     ap.add_argument("--cpu-tokens", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-40b", action="store_true",
+                    help="skip the config-5 (sharded 40B) record of the default run")
+    ap.add_argument("--no-model7b", action="store_true",
+                    help="skip the config-4 (full 7B model) record of the default run")
     ap.add_argument("--only", choices=["prefill", "decode"], default=None,
                     help="run one workload (small profiling cases)")
     ap.add_argument("--batch", type=int, default=PREFILL_B, help="prefill sequences per rank")
@@ -896,7 +944,7 @@ def main():
         from datetime import timedelta
 
         kw = {}
-        if args.workload == "tp40b":  # collectives overlap compute: schedule their CTAs first
+        if args.workload in ("tp40b", "triple"):  # collectives overlap compute: their CTAs first
             opts = dist.ProcessGroupNCCL.Options()
             opts.is_high_priority_stream = True
             kw["pg_options"] = opts
@@ -1006,6 +1054,20 @@ def main():
                "sample": f"1 x {args.cpu_tokens} ACGT tokens through the triple (oracle port, "
                          f"in_proj as bf16 GEMM on dequantised e4m3 weights), median of 3"}
 
+    model7b = None
+    if rank == 0 and world == 1 and not args.no_model7b:
+        ml = run_model7b(args, device, quiet=True)
+        model7b = {"workload": ml["config"]["workload"], "tok_per_s": ml["value"],
+                   "mean_nll": ml["mean_nll"], "ms": ml["ms_per_step"],
+                   "sequences": ml["config"]["sequences"], "tokens": ml["config"]["tokens"]}
+        torch.cuda.empty_cache()
+
+    sharded = None
+    if not args.no_40b:
+        del layers
+        torch.cuda.empty_cache()
+        sharded = sharded_40b_record(args, world, rank, device, dist_ok)
+
     launches_per_step = 5 + 5 + 8  # quant+gemm+core(2 or 5)+gemm per layer
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
@@ -1029,6 +1091,8 @@ def main():
                                       "bf16_tflops": bf16_peak, "hbm_gbs": hbm},
                      "triple_t_roof_ms": t_roof * 1e3, "triple_frac": t_roof * 1e3 / t_step},
         "decode": decode,
+        "config4": model7b,
+        "sharded_40b": sharded,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
