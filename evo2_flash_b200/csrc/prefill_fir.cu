@@ -79,7 +79,7 @@ struct FirShared {
     uint4 ys[FIR_CG * FIR_YS_CH];
     bf16 wpad[FIR_CG][K + 128];
   };
-  uint32_t zh[2][FIR_WORDS];             // z rows (r-2, r-1) before the tile
+  uint32_t zh[2][2][FIR_WORDS];          // z rows (r-2, r-1) before the tile, [tile parity]
   bf162 sw[3][3][FIR_PAIRS];             // short taps [column x2/x1/v][tap][pair]
   bf162 dsm[FIR_PAIRS];
 };
@@ -170,13 +170,14 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) {
 
 // The interleaved triple words of one channel pair -> (x2, x1, v) bf16x2 pairs.
 // Words: w0 = (x2_a, x1_a), w1 = (v_a, x2_b), w2 = (x1_b, v_b).
-__device__ __forceinline__ void split_triples(uint32_t w0, uint32_t w1, uint32_t w2, bf162& x2,
-                                              bf162& x1, bf162& v) {
-  x2 = as_bf162(__byte_perm(w0, w1, 0x7610));
+__device__ __forceinline__ bf162 split_x2(uint32_t w0, uint32_t w1) {
+  return as_bf162(__byte_perm(w0, w1, 0x7610));
+}
+__device__ __forceinline__ void split_x1v(uint32_t w0, uint32_t w1, uint32_t w2, bf162& x1,
+                                          bf162& v) {
   x1 = as_bf162(__byte_perm(w0, w2, 0x5432));
   v = as_bf162(__byte_perm(w1, w2, 0x7610));
 }
-
 // Tiles walk the CTA's rows [r0, r1) and never straddle a segment boundary.
 struct TileIt {
   int r, n, j;
@@ -194,15 +195,23 @@ __device__ __forceinline__ TileIt tile_at(const hyena_prefill_args& A, int r, in
 
 // Issues tile t's z rows into buffer buf and closes one cp.async group (empty
 // when t.n == 0, so that every loop iteration commits exactly one group).
+// Thread (group gi, row rin, chunk v) copies rows 8 gi + rin + 40 k: row
+// offsets in the gapped tile then advance by a constant.
 template <int K>
 __device__ __forceinline__ void prefetch_tile(FirShared<K>& S, const hyena_prefill_args& A,
                                               const TileIt& t, int buf, int c0) {
-  const bf16* z = static_cast<const bf16*>(A.z);
-  constexpr int VPR = FIR_WORDS * 4 / 16;  // 16-byte vectors per row
-  for (int i = threadIdx.x; i < t.n * VPR; i += FIR_THREADS) {
-    const int row = i / VPR, v = i % VPR;
-    cp_async16(&S.zt[buf][zrow(row) + 4 * v],
-               reinterpret_cast<const uint4*>(z + (long long)(t.r + row) * A.ldz + 3 * c0) + v);
+  constexpr int VPR = FIR_WORDS * 4 / 16;                      // 16-byte chunks per row
+  constexpr int PASS = (FIR_THREADS / (8 * VPR)) * 8;          // rows per pass
+  constexpr int DST_STEP = PASS * FIR_WORDS + 8 * (PASS / 8);  // zrow(r + PASS) - zrow(r)
+  const int tid = threadIdx.x;
+  if (tid < PASS * VPR) {
+    const int v = tid % VPR;
+    int r = 8 * (tid / (8 * VPR)) + (tid % (8 * VPR)) / VPR;
+    uint32_t* dst = &S.zt[buf][zrow(r) + 4 * v];
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(A.z) +
+                                                      (long long)(t.r + r) * A.ldz + 3 * c0) + v;
+    const long long step = (long long)PASS * A.ldz / 8;  // in 16-byte units
+    for (; r < t.n; r += PASS, dst += DST_STEP, src += step) cp_async16(dst, src);
   }
   cp_async_commit();
 }
@@ -270,20 +279,20 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
 
   // ---- W fragments of this warp's two channels (A operand of m16n8k16):
   // a0a1 (i = g, d0 + {0,1}), a2a3 (i = g + 8, d0 + {0,1}), a4a5 / a6a7 the same at d0 + 8,
-  // with d0 = DB0 + 16 ks + 2q.
-  uint32_t af[2][NA][4];
+  // with d0 = DB0 + 16 ks + 2q.  W(i, d) depends on d - i only, so with
+  // word(m) = (W(g, DB0 + 2q + 8 (m - 1)), the next tap): a0a1 = a6a7 = word(2 ks + 1),
+  // a2a3 = word(2 ks), a4a5 = word(2 ks + 2); NW distinct words cover every k-step.
+  constexpr int NW = 2 * NA + 1;
+  uint32_t wv[2][NW];
   {
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const bf16* wc = &S.wpad[2 * warp + cc][FIR_WOFF + K - 1];  // wc[d - i] = W(i, d)
 #pragma unroll
-      for (int ks = 0; ks < NA; ++ks) {
-        const int d0 = DB0 + 16 * ks + 2 * q;
-        af[cc][ks][0] = pack_bf16(wc[d0 - g], wc[d0 + 1 - g]);
-        af[cc][ks][1] = pack_bf16(wc[d0 - g - 8], wc[d0 + 1 - g - 8]);
-        af[cc][ks][2] = pack_bf16(wc[d0 + 8 - g], wc[d0 + 9 - g]);
-        af[cc][ks][3] = pack_bf16(wc[d0 + 8 - g - 8], wc[d0 + 9 - g - 8]);
+      for (int m = 0; m < NW; ++m) {
+        const int off = DB0 + 2 * q - g + 8 * (m - 1);
+        wv[cc][m] = pack_bf16(wc[off], wc[off + 1]);
       }
     }
   }
@@ -294,6 +303,7 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
   const int g0 = rg * FIR_RPT;
   bf16* ub_h = reinterpret_cast<bf16*>(S.ub);
   int cur_seg = -1;
+  int zc = 0;  // the zh buffer holding the current tile's z history
 
   while (t.n > 0) {
     const TileIt nt = tile_at(A, t.r + t.n, r1, t.j);
@@ -340,7 +350,7 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         const long long tr = (long long)t.r - 2 + q;
         const uint32_t lo = bf16_bits(z_at(A, seg, tr, 3 * c0 + 2 * wd));
         const uint32_t hi = bf16_bits(z_at(A, seg, tr, 3 * c0 + 2 * wd + 1));
-        S.zh[q][wd] = lo | (hi << 16);
+        S.zh[zc][q][wd] = lo | (hi << 16);
       }
     }
     cp_async_wait<FIR_STAGES - 1>();  // this tile's group (one group is committed per tile)
@@ -348,37 +358,35 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
 
     const int n = t.n, r = t.r;
     const uint32_t* zt = S.zt[buf];
-    // ---- gate phase: K=3 short filter on a channel pair over 8 consecutive rows
-    uint32_t x2r[FIR_RPT];
+    // rows g0 - 2, g0 - 1 of this thread's channel pair (z history at g0 = 0)
+    const uint32_t* zga = g0 >= 2 ? &zt[zrow(g0 - 2) + 3 * pp] : &S.zh[zc][g0][3 * pp];
+    const uint32_t* zgb = g0 >= 1 ? &zt[zrow(g0 - 1) + 3 * pp] : &S.zh[zc][1][3 * pp];
+    const uint32_t* zg = &zt[zrow(g0) + 3 * pp];  // rows g0.. of one 8-row group
+    // ---- gate phase: K=3 short filter of the x1 and v columns on a channel pair
+    // over 8 consecutive rows, u = x1 * v (x2 is filtered in the store phase)
     if (g0 < n) {
-      bf162 w[3][3];
+      bf162 w[2][3];
 #pragma unroll
-      for (int c = 0; c < 3; ++c)
+      for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int k = 0; k < 3; ++k) w[c][k] = S.sw[c][k][pp];
-      bf162 h2[3], h1[3];
-      {
-        const uint32_t* a = g0 >= 2 ? &zt[zrow(g0 - 2) + 3 * pp] : &S.zh[g0][3 * pp];
-        const uint32_t* b = g0 >= 1 ? &zt[zrow(g0 - 1) + 3 * pp] : &S.zh[1][3 * pp];
-        split_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
-        split_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
-      }
+        for (int k = 0; k < 3; ++k) w[c][k] = S.sw[c + 1][k][pp];
+      bf162 h2[2], h1[2];
+      split_x1v(zga[0], zga[1], zga[2], h2[0], h2[1]);
+      split_x1v(zgb[0], zgb[1], zgb[2], h1[0], h1[1]);
       uint32_t uu[FIR_RPT];
-      const uint32_t* zg = &zt[zrow(g0) + 3 * pp];  // rows g0.. of one 8-row group
 #pragma unroll
       for (int i = 0; i < FIR_RPT; ++i) {
         const uint32_t* zr = zg + i * FIR_WORDS;
-        bf162 cur[3], o[3];
-        split_triples(zr[0], zr[1], zr[2], cur[0], cur[1], cur[2]);
+        bf162 cur[2], o[2];
+        split_x1v(zr[0], zr[1], zr[2], cur[0], cur[1]);
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
+        for (int c = 0; c < 2; ++c) {
           o[c] = short_tap2(h2[c], h1[c], cur[c], w[c][0], w[c][1], w[c][2]);
           h2[c] = h1[c];
           h1[c] = cur[c];
         }
         // rows past the tile read stale shared memory: their u must not reach the buffer
-        uu[i] = g0 + i < n ? as_u32(__hmul2(o[1], o[2])) : 0u;
-        x2r[i] = as_u32(o[0]);
+        uu[i] = g0 + i < n ? as_u32(__hmul2(o[0], o[1])) : 0u;
       }
       // channel pairs by row -> 8 consecutive rows per channel
       uint4 ua, ub;
@@ -412,8 +420,16 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         for (int ks = 0; ks < NKS; ++ks) {
           uint32_t b0, b1;
           ldsm_x2(b0, b1, &S.ub[ch * G::UCH + lbase + 5 * (ks >> 1) + 2 * (ks & 1)]);
-          if (ks < NA) mma_bf16(acc[0], af[cc][ks], b0, b1);
-          if (ks >= 1) mma_bf16(acc[1], af[cc][ks - 1], b0, b1);
+          if (ks < NA) {
+            const uint32_t a[4] = {wv[cc][2 * ks + 1], wv[cc][2 * ks], wv[cc][2 * ks + 2],
+                                   wv[cc][2 * ks + 1]};
+            mma_bf16(acc[0], a, b0, b1);
+          }
+          if (ks >= 1) {
+            const uint32_t a[4] = {wv[cc][2 * ks - 1], wv[cc][2 * ks - 2], wv[cc][2 * ks],
+                                   wv[cc][2 * ks - 1]};
+            mma_bf16(acc[1], a, b0, b1);
+          }
         }
         stsm_x4_trans(&S.ys[ch * FIR_YS_CH + sbase], pack_rn(acc[0][0], acc[0][1]),
                       pack_rn(acc[0][2], acc[0][3]), pack_rn(acc[1][0], acc[1][1]),
@@ -436,33 +452,41 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         ubw[0] = ub.x; ubw[1] = ub.y; ubw[2] = ub.z; ubw[3] = ub.w;
       }
       const bf162 d2 = S.dsm[pp];
+      const bf162 wx0 = S.sw[0][0][pp], wx1 = S.sw[0][1][pp], wx2 = S.sw[0][2][pp];
+      bf162 x2h2 = split_x2(zga[0], zga[1]), x2h1 = split_x2(zgb[0], zgb[1]);
       bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + g0) * A.ldo + c0) + pp;
       const long long ld2 = A.ldo / 2;
 #pragma unroll
       for (int i = 0; i < FIR_RPT; ++i) {
+        const bf162 x2c = split_x2(zg[i * FIR_WORDS], zg[i * FIR_WORDS + 1]);
+        const bf162 x2 = short_tap2(x2h2, x2h1, x2c, wx0, wx1, wx2);
+        x2h2 = x2h1;
+        x2h1 = x2c;
         if (g0 + i < n) {
           const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
           bf162 y = as_bf162(__byte_perm(yaw[i >> 1], ybw[i >> 1], sel));
           // D*u is rounded to bf16 before the add, as torch does: the _rn
           // multiply keeps the compiler from fusing the two into one bf16 FMA
           if (has_d) y = __hadd2(y, __hmul2_rn(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
-          outp[i * ld2] = __hmul2(as_bf162(x2r[i]), y);
+          outp[i * ld2] = __hmul2(x2, y);
         }
       }
     }
-    // ---- z history for the next tile of this segment (z buffer and zh only)
+    // ---- z history for the next tile of this segment, into the other zh
+    // buffer (the store phase may still read this tile's)
     if (tid < FIR_WORDS) {
       uint32_t h0v, h1v;
       if (n >= 2) {
         h0v = zt[zrow(n - 2) + tid];
         h1v = zt[zrow(n - 1) + tid];
       } else {
-        h0v = S.zh[1][tid];
+        h0v = S.zh[zc][1][tid];
         h1v = zt[zrow(0) + tid];
       }
-      S.zh[0][tid] = h0v;
-      S.zh[1][tid] = h1v;
+      S.zh[zc ^ 1][0][tid] = h0v;
+      S.zh[zc ^ 1][1][tid] = h1v;
     }
+    zc ^= 1;
     // ---- the tile's last HALO rows of u become the next tile's history
     // (read from rows the store phase does not touch; written over rows no
     // one reads until the next tile's tap phase)
@@ -584,7 +608,7 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   // Rows per CTA: a multiple of the tile, long enough that the (K-1)-row halo is
   // a small fraction, short enough to fill the 148 SMs several times over.
   const int groups = P.H / FIR_CG;
-  int rows = K > 16 ? 2048 : 1024;
+  int rows = 4096;
   const long long want_ctas = 148LL * 8;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
   while ((A.T + rows - 1) / rows > 65535) rows *= 2;

@@ -137,11 +137,13 @@ struct HclShared {
   uint32_t zt[HCL_STAGES][HCL_ZT_WORDS];  // z tiles, bf16x2 words
   uint4 ub[HCL_CG * HCL_CH];               // u by (channel, tile row), bf16
   uint4 ys[HCL_CG * HCL_CH];               // y by (channel, tile row), bf16
-  float pw[HCL_CG][HCL_S][HCL_NJ + 1];     // (p_s^32)^e, e = 0..16
+  // (p_s^32)^e, e = 0..16; a stride of 20 per mode keeps the scan's lanes
+  // (mode 2q + c, power g) on 32 different banks
+  float pw[HCL_CG][HCL_S][20];
   float pole[HCL_CG][HCL_S];               // p_s
   float hf[HCL_CG][HCL_C];                 // modal filter h[l], l < 32
   float sfin[HCL_CG][HCL_S];               // S_in of a segment's last chunk
-  uint32_t zh[2][HCL_WORDS];               // z rows (r-2, r-1) before the tile
+  uint32_t zh[2][2][HCL_WORDS];            // z rows (r-2, r-1) before the tile, [tile parity]
   bf162 sw[3][3][HCL_PAIRS];               // short taps [column][tap][pair]
   bf162 dsm[HCL_PAIRS];
 };
@@ -211,23 +213,35 @@ __device__ __forceinline__ float hz_at(const hyena_prefill_args& A, const RangeC
               (long long)col * A.conv_state.dim_stride);
 }
 
-__device__ __forceinline__ void hsplit_triples(uint32_t w0, uint32_t w1, uint32_t w2, bf162& x2,
-                                               bf162& x1, bf162& v) {
-  x2 = as_bf162(__byte_perm(w0, w1, 0x7610));
+// The interleaved triple words of one channel pair, w0 = (x2_a, x1_a),
+// w1 = (v_a, x2_b), w2 = (x1_b, v_b) -> bf16x2 pairs of one column.
+__device__ __forceinline__ bf162 hsplit_x2(uint32_t w0, uint32_t w1) {
+  return as_bf162(__byte_perm(w0, w1, 0x7610));
+}
+__device__ __forceinline__ void hsplit_x1v(uint32_t w0, uint32_t w1, uint32_t w2, bf162& x1,
+                                           bf162& v) {
   x1 = as_bf162(__byte_perm(w0, w2, 0x5432));
   v = as_bf162(__byte_perm(w1, w2, 0x7610));
 }
 
 // Issues the z rows [r, r + n) of this CTA's channels into buffer buf and
-// closes one cp.async group (empty when n == 0).
-__device__ __forceinline__ void hcl_prefetch(HclShared& S, const hyena_prefill_args& A, int r,
+// closes one cp.async group (empty when n == 0).  Thread (group gi, row rin,
+// chunk v) copies rows 8 gi + rin + 80 k: row offsets in the gapped tile then
+// advance by a constant.
+__device__ __forceinline__ void hcl_prefetch(HclShared& S, const hyena_prefill_args& A, int r0,
                                              int n, int buf, int c0) {
-  const bf16* z = static_cast<const bf16*>(A.z);
-  constexpr int VPR = HCL_WORDS * 4 / 16;  // 16-byte vectors per row
-  for (int i = threadIdx.x; i < n * VPR; i += HCL_THREADS) {
-    const int row = i / VPR, v = i % VPR;
-    cp_async16(&S.zt[buf][hzrow(row) + 4 * v],
-               reinterpret_cast<const uint4*>(z + (long long)(r + row) * A.ldz + 3 * c0) + v);
+  constexpr int VPR = HCL_WORDS * 4 / 16;                      // 16-byte chunks per row
+  constexpr int PASS = (HCL_THREADS / (8 * VPR)) * 8;          // rows per pass
+  constexpr int DST_STEP = PASS * HCL_WORDS + 4 * (PASS / 8);  // hzrow(r + PASS) - hzrow(r)
+  const int tid = threadIdx.x;
+  if (tid < PASS * VPR) {
+    const int v = tid % VPR;
+    int r = 8 * (tid / (8 * VPR)) + (tid % (8 * VPR)) / VPR;
+    uint32_t* dst = &S.zt[buf][hzrow(r) + 4 * v];
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(A.z) +
+                                                      (long long)(r0 + r) * A.ldz + 3 * c0) + v;
+    const long long step = (long long)PASS * A.ldz / 8;  // in 16-byte units
+    for (; r < n; r += PASS, dst += DST_STEP, src += step) cp_async16(dst, src);
   }
   cp_async_commit();
 }
@@ -296,7 +310,7 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
     for (int i = tid; i < 2 * HCL_WORDS; i += HCL_THREADS) {
       const int q = i / HCL_WORDS, wd = i % HCL_WORDS;
       const long long t = (long long)c.row0 - 2 + q;
-      S.zh[q][wd] = hbits(hz_at(A, c, t, 3 * c0 + 2 * wd)) |
+      S.zh[0][q][wd] = hbits(hz_at(A, c, t, 3 * c0 + 2 * wd)) |
                     (hbits(hz_at(A, c, t, 3 * c0 + 2 * wd + 1)) << 16);
     }
   }
@@ -372,6 +386,7 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
   bf16* out = static_cast<bf16*>(A.out);
   const bool has_d = P.D != nullptr;
   int buf = 0;
+  int zc = 0;  // the zh buffer holding the current tile's z history
 
   for (int it = 0; it < ntiles; ++it) {
     const int r = c.row0 + it * HCL_BT;
@@ -386,37 +401,35 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
     __syncthreads();
     const uint32_t* zt = S.zt[buf];
 
-    // ---- gate phase: K=3 short filter on a channel pair over 8 consecutive rows
-    uint32_t x2r[HCL_RPT];
+    // rows g0 - 2, g0 - 1 of this thread's channel pair (z history at g0 = 0)
+    const uint32_t* zga = g0 >= 2 ? &zt[hzrow(g0 - 2) + 3 * pp] : &S.zh[zc][g0][3 * pp];
+    const uint32_t* zgb = g0 >= 1 ? &zt[hzrow(g0 - 1) + 3 * pp] : &S.zh[zc][1][3 * pp];
+    const uint32_t* zg = &zt[hzrow(g0) + 3 * pp];  // rows g0.. of one 8-row group
+    // ---- gate phase: K=3 short filter of the x1 and v columns on a channel pair
+    // over 8 consecutive rows, u = x1 * v (x2 is filtered in the store phase)
     if (g0 < n) {
-      bf162 w[3][3];
+      bf162 w[2][3];
 #pragma unroll
-      for (int cc = 0; cc < 3; ++cc)
+      for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
-        for (int k = 0; k < 3; ++k) w[cc][k] = S.sw[cc][k][pp];
-      bf162 h2[3], h1[3];
-      {
-        const uint32_t* a = g0 >= 2 ? &zt[hzrow(g0 - 2) + 3 * pp] : &S.zh[g0][3 * pp];
-        const uint32_t* b = g0 >= 1 ? &zt[hzrow(g0 - 1) + 3 * pp] : &S.zh[1][3 * pp];
-        hsplit_triples(a[0], a[1], a[2], h2[0], h2[1], h2[2]);
-        hsplit_triples(b[0], b[1], b[2], h1[0], h1[1], h1[2]);
-      }
+        for (int k = 0; k < 3; ++k) w[cc][k] = S.sw[cc + 1][k][pp];
+      bf162 h2[2], h1[2];
+      hsplit_x1v(zga[0], zga[1], zga[2], h2[0], h2[1]);
+      hsplit_x1v(zgb[0], zgb[1], zgb[2], h1[0], h1[1]);
       uint32_t uu[HCL_RPT];
-      const uint32_t* zg = &zt[hzrow(g0) + 3 * pp];  // rows g0.. of one 8-row group
 #pragma unroll
       for (int i = 0; i < HCL_RPT; ++i) {
         const uint32_t* zr = zg + i * HCL_WORDS;
-        bf162 cur[3], o[3];
-        hsplit_triples(zr[0], zr[1], zr[2], cur[0], cur[1], cur[2]);
+        bf162 cur[2], o[2];
+        hsplit_x1v(zr[0], zr[1], zr[2], cur[0], cur[1]);
 #pragma unroll
-        for (int cc = AGG ? 1 : 0; cc < 3; ++cc) {
+        for (int cc = 0; cc < 2; ++cc) {
           o[cc] = short_tap2(h2[cc], h1[cc], cur[cc], w[cc][0], w[cc][1], w[cc][2]);
           h2[cc] = h1[cc];
           h1[cc] = cur[cc];
         }
         // rows past the range read stale shared memory: their u must be zero
-        uu[i] = g0 + i < n ? as_u32(__hmul2(o[1], o[2])) : 0u;
-        if (!AGG) x2r[i] = as_u32(o[0]);
+        uu[i] = g0 + i < n ? as_u32(__hmul2(o[0], o[1])) : 0u;
       }
       uint4 ua, ubv;
       ua.x = __byte_perm(uu[0], uu[1], 0x5410); ubv.x = __byte_perm(uu[0], uu[1], 0x7632);
@@ -561,10 +574,16 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
         const uint32_t yaw[4] = {ya.x, ya.y, ya.z, ya.w}, ybw[4] = {yb.x, yb.y, yb.z, yb.w};
         const uint32_t uaw[4] = {ua.x, ua.y, ua.z, ua.w}, ubw[4] = {ubv.x, ubv.y, ubv.z, ubv.w};
         const bf162 d2 = S.dsm[pp];
+        const bf162 wx0 = S.sw[0][0][pp], wx1 = S.sw[0][1][pp], wx2 = S.sw[0][2][pp];
+        bf162 x2h2 = hsplit_x2(zga[0], zga[1]), x2h1 = hsplit_x2(zgb[0], zgb[1]);
         bf162* outp = reinterpret_cast<bf162*>(out + (long long)(r + g0) * A.ldo + c0) + pp;
         const long long ld2 = A.ldo / 2;
 #pragma unroll
         for (int i = 0; i < HCL_RPT; ++i) {
+          const bf162 x2c = hsplit_x2(zg[i * HCL_WORDS], zg[i * HCL_WORDS + 1]);
+          const bf162 x2 = short_tap2(x2h2, x2h1, x2c, wx0, wx1, wx2);
+          x2h2 = x2h1;
+          x2h1 = x2c;
           if (g0 + i < n) {
             const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
             bf162 y = as_bf162(__byte_perm(yaw[i >> 1], ybw[i >> 1], sel));
@@ -572,16 +591,18 @@ hcl_tc_kernel(const hyena_layer_params P, const hyena_prefill_args A, HclPlan W)
             // multiply keeps the compiler from fusing the two into one bf16 FMA
             if (has_d)
               y = __hadd2(y, __hmul2_rn(d2, as_bf162(__byte_perm(uaw[i >> 1], ubw[i >> 1], sel))));
-            outp[i * ld2] = __hmul2(as_bf162(x2r[i]), y);
+            outp[i * ld2] = __hmul2(x2, y);
           }
         }
       }
     }
-    // ---- z history for the next tile
+    // ---- z history for the next tile, into the other zh buffer (the store
+    // phase may still read this tile's)
     if (tid < HCL_WORDS && n == HCL_BT) {
-      S.zh[0][tid] = zt[hzrow(HCL_BT - 2) + tid];
-      S.zh[1][tid] = zt[hzrow(HCL_BT - 1) + tid];
+      S.zh[zc ^ 1][0][tid] = zt[hzrow(HCL_BT - 2) + tid];
+      S.zh[zc ^ 1][1][tid] = zt[hzrow(HCL_BT - 1) + tid];
     }
+    zc ^= 1;
     buf = (buf + 1) % HCL_STAGES;
   }
   cp_async_wait<0>();
