@@ -110,7 +110,7 @@ __device__ __forceinline__ void stsm_x4_trans(void* p, uint32_t r0, uint32_t r1,
 // d += a . b, m16n8k16, bf16 operands, fp32 accumulators.
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -416,10 +416,14 @@ fir_prefill_kernel(const hyena_layer_params P, const hyena_prefill_args A, int r
         for (int m = 0; m < 2; ++m)
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[m][e] = 0.0f;
+        // every U fragment of the channel in flight before the first product
+        uint32_t bu[NKS][2];
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks)
+          ldsm_x2(bu[ks][0], bu[ks][1], &S.ub[ch * G::UCH + lbase + 5 * (ks >> 1) + 2 * (ks & 1)]);
 #pragma unroll
         for (int ks = 0; ks < NKS; ++ks) {
-          uint32_t b0, b1;
-          ldsm_x2(b0, b1, &S.ub[ch * G::UCH + lbase + 5 * (ks >> 1) + 2 * (ks & 1)]);
+          const uint32_t b0 = bu[ks][0], b1 = bu[ks][1];
           if (ks < NA) {
             const uint32_t a[4] = {wv[cc][2 * ks + 1], wv[cc][2 * ks], wv[cc][2 * ks + 2],
                                    wv[cc][2 * ks + 1]};

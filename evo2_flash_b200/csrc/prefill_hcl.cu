@@ -173,7 +173,7 @@ __device__ __forceinline__ void hstsm_x4(void* p, uint32_t r0, uint32_t r1, uint
 }
 // d += a . b, m16n8k16, bf16 operands, fp32 accumulators.
 __device__ __forceinline__ void hmma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
