@@ -529,6 +529,16 @@ H40 = 8192
 TP_TOKENS = 262144
 
 
+def collective_used(layers):
+    """Which all-reduce the channel-sharded out_proj of these layers ran."""
+    from evo2_flash_b200 import parallel
+
+    red = [r for r in parallel._REDUCERS.values() if r]
+    if layers[0].tp_collective == "nccl" or not red:
+        return "nccl all-reduce"
+    return f"in-switch NVLS all-reduce kernel ({red[0].num_ctas} CTAs, collective stream)"
+
+
 def run_tp40b(args, world, rank, device, dist_ok, quiet=False):
     """40B-shape triple, channel-sharded over `world` ranks; chunked prefill with
     the row-parallel all-reduces in flight under the following chunks, then
@@ -561,7 +571,8 @@ def run_tp40b(args, world, rank, device, dist_ok, quiet=False):
     for i, (kind, k) in enumerate(TRIPLE):
         t = mixer_tensors(kind, H40, k, 200 + i, fp8=True, device=device)
         t["in_proj.input_scale"] = sx
-        kw = dict(tp_rank=rank, tp_size=world, tp_group=group, device=device)
+        kw = dict(tp_rank=rank, tp_size=world, tp_group=group, device=device,
+                  tp_collective=args.tp_collective)
         m = (HyenaIIRMixer(cfg, i, prefix=f"tp.{i}", **kw) if kind == "hcl"
              else HyenaFIRMixer(cfg, i, prefix=f"tp.{i}", k_inner=k, **kw))
         m.load_full_weights(t)
@@ -641,6 +652,7 @@ def run_tp40b(args, world, rank, device, dist_ok, quiet=False):
                    "hidden": H40, "global_batch": 1, "seq_len": TP_TOKENS,
                    "parallelism": f"tp{world}", "prefill_chunk": chunk,
                    "gemm_sms_left_to_collectives": reserve,
+                   "collective": collective_used(layers) if world > 1 else None,
                    "launch_chaining": bool(args.tp_chaining) or world == 1,
                    "l2": "inputs larger than L2 (x 4.3 GB)"},
         "tok_per_s_per_gpu": value / world,
@@ -880,6 +892,18 @@ def sharded_40b_record(args, world, rank, device, dist_ok):
     return rec
 
 
+def release_reducers():
+    """Checks every in-switch reducer's error word (a cross-rank wait that
+    expired) and frees their symmetric buffers, before the process group goes."""
+    from evo2_flash_b200 import parallel
+
+    for red in parallel._REDUCERS.values():
+        if red:
+            red.check()
+    parallel._REDUCERS.clear()
+    torch.cuda.synchronize()
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -907,6 +931,8 @@ def main():
     ap.add_argument("--tp-decode-steps", type=int, default=256)
     ap.add_argument("--tp-reserve-sms", type=int, default=0,
                     help="tp40b with N > 1: SMs the projection GEMMs leave to the all-reduces")
+    ap.add_argument("--tp-collective", choices=["auto", "nvls", "nccl"], default="auto",
+                    help="tp40b: the out_proj all-reduce (in-switch kernel or NCCL)")
     ap.add_argument("--tp-chaining", type=int, default=1,
                     help="tp40b with N > 1: programmatic dependent launch between kernels (1/0)")
     args = ap.parse_args()
@@ -959,6 +985,7 @@ def main():
         return
     if args.workload in ("tp40b", "cp40b"):
         (run_tp40b if args.workload == "tp40b" else run_cp40b)(args, world, rank, device, dist_ok)
+        release_reducers()
         if dist_ok:
             dist.barrier()
             dist.destroy_process_group()
@@ -1100,6 +1127,7 @@ def main():
     }
     if rank == 0:
         print(json.dumps(line))
+    release_reducers()
     if dist_ok:
         dist.barrier()
         dist.destroy_process_group()

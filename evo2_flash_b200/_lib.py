@@ -13,7 +13,7 @@ from ._build import LIB_PATH
 
 HYENA_KIND_FIR = 0
 HYENA_KIND_IIR = 1
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 class StateView(C.Structure):
@@ -128,6 +128,9 @@ SIGNATURES = {
     "hyena_set_gemm_max_ctas": (None, [C.c_int32]),
     "hyena_gemm_wait_timeouts": (C.c_int, [C.POINTER(C.c_int32), C.c_int32]),
     "hyena_set_launch_chaining": (None, [C.c_int32]),
+    "hyena_nvls_allreduce_bf16": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int32,
+                                            C.c_int32, C.c_uint32, C.c_int32, C.c_void_p,
+                                            C.c_void_p]),
     "hyena_spec_accepted": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p]),

@@ -208,7 +208,7 @@ class HyenaMixerBase(nn.Module):
     def __init__(self, config, layer_idx: int, model_config=None, cache_config=None,
                  prefix: str = "", quant_config=None, *, num_spec: int | None = None,
                  tp_rank: int = 0, tp_size: int = 1, tp_group=None, device=None,
-                 compilation_config=None):
+                 compilation_config=None, tp_collective: str = "auto"):
         super().__init__()
         self.config = config
         self.layer_idx = layer_idx
@@ -220,6 +220,11 @@ class HyenaMixerBase(nn.Module):
             raise ValueError(f"hidden size {h} does not split over {tp_size} ranks")
         self.hidden_full = h
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        # the row-parallel out_proj's all-reduce: "nvls" (in-switch, our kernel),
+        # "nccl", or "auto" (nvls where the GPUs have NVLink multicast)
+        if tp_collective not in ("auto", "nvls", "nccl"):
+            raise ValueError(f"tp_collective must be auto, nvls or nccl, got {tp_collective!r}")
+        self.tp_collective = tp_collective
         self.hidden = h // tp_size
         hl = self.hidden
         self.k_short = config.short_filter_length
@@ -484,7 +489,21 @@ class HyenaMixerBase(nn.Module):
         """out_proj of g; with `out` (at least g's rows) the result is written
         into its first rows.  Channel-sharded: the partial sums (rank 0's with the
         bias from its GEMM epilogue) are all-reduced, left in flight when
-        async_reduce (PendingReduce)."""
+        async_reduce.  With the in-switch collective the GEMM writes the partial
+        into the group reducer's buffer ring and the result is a view into that
+        ring, valid until 32 further channel-sharded out_projs of the group have
+        been started (every caller here consumes it before then)."""
+        if self.tp_size > 1 and out is None and self.tp_collective != "nccl":
+            from .parallel import nvls_reducer
+
+            red = nvls_reducer(self.tp_group, g.shape[0] * self.hidden_full, g.device)
+            if red is None and self.tp_collective == "nvls":
+                raise RuntimeError("tp_collective='nvls' but the GPUs have no NVLink multicast")
+            if red is not None:
+                k, buf = red.buffer(g.shape[0], self.hidden_full)
+                self.out_proj(g, out=buf)
+                pend = red.reduce_async(k, buf)
+                return pend if async_reduce else pend.wait()
         y, _ = self.out_proj(g, out=None if out is None else out[: g.shape[0]])
         full = y if out is None else out
         if self.tp_size > 1:

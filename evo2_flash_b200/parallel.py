@@ -91,3 +91,114 @@ def all_reduce_partial_async(out: torch.Tensor, bias: torch.Tensor | None, group
     """all_reduce_partial with the collective left in flight (see PendingReduce)."""
     work = dist.all_reduce(out, group=group, async_op=True)
     return PendingReduce(out, bias, work, finish)
+
+
+class PendingNvls:
+    """A row-parallel out_proj whose in-switch all-reduce runs on the reducer's
+    collective stream; wait() orders the caller's stream after it and returns
+    the reduced rows (a view into the reducer's buffer ring, valid until `slots`
+    further reductions have been started)."""
+
+    def __init__(self, out, done, finish=None):
+        self._out, self._ev, self._finish = out, done, finish
+        self._done = None
+
+    def wait(self) -> torch.Tensor:
+        if self._done is None:
+            torch.cuda.current_stream().wait_event(self._ev)
+            self._done = self._finish(self._out) if self._finish is not None else self._out
+        return self._done
+
+
+class NvlsReducer:
+    """In-switch (NVLink SHARP) all-reduce of row-parallel partial sums for one
+    process group (hyena_nvls_allreduce_bf16).
+
+    The out_proj GEMM of every rank writes its partial straight into the next
+    buffer of a ring of symmetric, multicast-mapped buffers; the reduction
+    kernel then runs on a high-priority collective stream with a few CTAs, so
+    it proceeds beside the next layer's or chunk's kernels instead of taking
+    whole SMs the way a ring all-reduce does.  A buffer is written again only
+    after this rank's previous reduction of it has finished, which (through the
+    kernel's closing handshake) means every rank has finished with it too.
+    Every rank must make the same calls in the same order."""
+
+    def __init__(self, group, max_elems: int, device, slots: int = 32, num_ctas: int = 16):
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.max_elems = (int(max_elems) + 7) // 8 * 8
+        self.slots, self.num_ctas = slots, num_ctas
+        self.buf = symm.empty((slots, self.max_elems), dtype=torch.bfloat16, device=device)
+        self.hdl = symm.rendezvous(self.buf, self.group.group_name)
+        if not self.hdl.multicast_ptr:
+            raise RuntimeError("NVLink multicast is not available for this group")
+        self.rank, self.world = self.hdl.rank, self.hdl.world_size
+        self.stream = torch.cuda.Stream(device=device, priority=-1)
+        self.epoch = 0
+        self.next = 0
+        self.done = [None] * slots
+        self.error = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def buffer(self, rows: int, cols: int):
+        """The next ring buffer as a (rows, cols) bf16 tensor, once this rank's
+        previous reduction of it has finished."""
+        n = rows * cols
+        if n > self.max_elems:
+            raise ValueError(f"{n} elements exceed the reducer's {self.max_elems}")
+        k = self.next
+        self.next = (k + 1) % self.slots
+        if self.done[k] is not None:
+            torch.cuda.current_stream().wait_event(self.done[k])
+        return k, self.buf[k, :n].view(rows, cols)
+
+    def reduce_async(self, k: int, t: torch.Tensor, finish=None) -> PendingNvls:
+        """Starts the all-reduce of ring buffer k (holding t) after the caller's
+        stream has produced it."""
+        from . import _lib
+
+        ready = torch.cuda.Event()
+        ready.record()
+        self.stream.wait_event(ready)
+        self.epoch += 1
+        n = t.numel()
+        n_pad = (n + 7) // 8 * 8
+        mc = self.hdl.multicast_ptr + k * self.max_elems * 2
+        _lib.check(_lib.load().hyena_nvls_allreduce_bf16(
+            _lib.C.c_void_p(mc), n_pad, _lib.C.c_void_p(self.hdl.signal_pad_ptrs_dev),
+            self.hdl.signal_pad_size, self.rank, self.world, self.epoch, self.num_ctas,
+            _lib.C.c_void_p(self.error.data_ptr()), _lib.C.c_void_p(self.stream.cuda_stream)),
+            "hyena_nvls_allreduce_bf16")
+        done = torch.cuda.Event()
+        done.record(self.stream)
+        self.done[k] = done
+        return PendingNvls(t, done, finish)
+
+    def check(self) -> None:
+        """Raises if a cross-rank wait of an earlier reduction expired (reads the
+        device error word: synchronises with the collective stream)."""
+        self.stream.synchronize()
+        if int(self.error.item()):
+            raise RuntimeError("NVLS all-reduce: a cross-rank wait expired (ranks out of step)")
+
+
+_REDUCERS: dict = {}
+
+
+def nvls_reducer(group, elems: int, device, slots: int = 32):
+    """The process-wide NvlsReducer of (group, device), grown to hold `elems`
+    per buffer (growing re-allocates: a collective call, made by every rank at
+    the same point because every rank runs the same layers), or None when the
+    group's GPUs have no NVLink multicast."""
+    key = (id(group), str(device))
+    red = _REDUCERS.get(key)
+    if red is False:
+        return None
+    if red is None or red.max_elems < elems:
+        try:
+            red = NvlsReducer(group, max(elems, 0 if red is None else red.max_elems), device, slots)
+        except RuntimeError:
+            _REDUCERS[key] = False
+            return None
+        _REDUCERS[key] = red
+    return red

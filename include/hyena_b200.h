@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define HYENA_ABI_VERSION 6
+#define HYENA_ABI_VERSION 7
 
 #if defined(__GNUC__)
 #define HYENA_API __attribute__((visibility("default")))
@@ -47,6 +47,7 @@ extern "C" {
 #define HYENA_FLAG_BLOCK_RANGE 1 /* a state block index was outside [0, num_blocks) */
 #define HYENA_FLAG_SEGMENT 2     /* query_start_loc was not non-decreasing / exceeded T */
 #define HYENA_FLAG_STAMP 4       /* a position stamp did not match the request position */
+#define HYENA_FLAG_COLLECTIVE 8  /* a cross-rank wait of a collective kernel expired */
 
 typedef struct hyena_state_view {
   void* data;            /* element (block 0, column 0, channel 0) */
@@ -127,6 +128,23 @@ HYENA_API int hyena_prefill(const hyena_layer_params* p, const hyena_prefill_arg
  * calls whose kernels overlap on the GPU race on it. */
 HYENA_API int hyena_prefill_noalloc(const hyena_layer_params* p, const hyena_prefill_args* a,
                                     void* stream);
+
+/* ---------------------------------------------------------------- channel-sharded out_proj
+ * In-switch (NVLink SHARP) all-reduce of the row-parallel out_proj partial sums,
+ * the "one all-reduce per block" of the channel-sharded mixer.  No counterpart in
+ * the reference, which has no tensor parallelism (evo2_flash/mixers.py:38-41);
+ * it stands where a NCCL all-reduce of the (T, H) bf16 partial would.
+ * multicast: the multicast address of a symmetric buffer holding n_elems bf16 on
+ * every rank (in place: every rank's buffer ends with the sum, accumulated in
+ * fp32 and rounded once); signal_pads: device array of the `world` ranks' signal
+ * pads (zero-initialised, signal_pad_bytes each, >= 8 * num_ctas * world bytes);
+ * epoch: nonzero, larger than every earlier call's on these pads.  All ranks make
+ * the same calls in the same order.  A cross-rank wait that expires (~1 s) sets
+ * HYENA_FLAG_COLLECTIVE in *error_flags and the kernel returns. */
+HYENA_API int hyena_nvls_allreduce_bf16(void* multicast, int64_t n_elems, void* const* signal_pads,
+                                        int64_t signal_pad_bytes, int32_t rank, int32_t world,
+                                        uint32_t epoch, int32_t num_ctas, int32_t* error_flags,
+                                        void* stream);
 
 /* ---------------------------------------------------------------- decode / verify
  * Replaces, for the decode rows of one step:

@@ -1,7 +1,8 @@
-"""Channel-sharded mixer modules on 2 GPUs over NCCL: rank r owns half the
-channels (its in_proj triples, filters and paged state), out_proj partial sums are
-all-reduced, and every step must match the unsharded mixer on one GPU.
-Skipped with fewer than 2 GPUs."""
+"""Channel-sharded mixer modules on 2 GPUs: rank r owns half the channels (its
+in_proj triples, filters and paged state), out_proj partial sums are all-reduced
+-- by NCCL, or by the in-switch NVLS kernel (hyena_nvls_allreduce_bf16) -- and
+every step must match the unsharded mixer on one GPU.  Skipped with fewer than 2
+GPUs; the NVLS case also without NVLink multicast."""
 
 import os
 import socket
@@ -25,12 +26,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _build(kind, k, dev, rank=0, world=1, group=None):
+def _build(kind, k, dev, rank=0, world=1, group=None, collective="auto"):
     from evo2_flash_b200 import HyenaFIRMixer, HyenaIIRMixer
 
     cfg = SimpleNamespace(hidden_size=H, short_filter_length=3, hcm_filter_length=128,
                           state_size=16, use_fp8_input_projections=False)
-    kw = dict(tp_rank=rank, tp_size=world, tp_group=group, device=dev)
+    kw = dict(tp_rank=rank, tp_size=world, tp_group=group, device=dev, tp_collective=collective)
     m = (HyenaIIRMixer(cfg, 0, prefix="tp", **kw) if kind == "hcl"
          else HyenaFIRMixer(cfg, 0, prefix="tp", k_inner=k, **kw))
     m.load_full_weights({kk: v.to(dev) for kk, v in random_params(kind, H, k, seed=23).items()})
@@ -58,35 +59,50 @@ def _run(m, dev):
     return outs
 
 
-def _worker(rank, world, kind, k, port, out_dir):
+def _worker(rank, world, kind, k, port, out_dir, collective):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     from datetime import timedelta
 
+    from evo2_flash_b200 import parallel
+
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=dev)
     try:
-        outs = _run(_build(kind, k, dev, rank, world, dist.group.WORLD), dev)
-        if rank == 0:
-            torch.save(outs, os.path.join(out_dir, "tp.pt"))
+        if collective == "nvls" and parallel.nvls_reducer(dist.group.WORLD, 1 << 17, dev) is None:
+            if rank == 0:
+                torch.save("no multicast", os.path.join(out_dir, "tp.pt"))
+        else:
+            m = _build(kind, k, dev, rank, world, dist.group.WORLD, collective)
+            outs = _run(m, dev)
+            if collective == "nvls":
+                parallel.nvls_reducer(dist.group.WORLD, 8, dev).check()
+            if rank == 0:
+                torch.save(outs, os.path.join(out_dir, "tp.pt"))
         dist.barrier()
     finally:
+        parallel._REDUCERS.clear()
+        torch.cuda.synchronize()
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("collective", ["nccl", "nvls"])
 @pytest.mark.parametrize("kind,k", [("hcm", 128), ("hcl", 16)])
-def test_tp2_matches_single_gpu(kind, k, tmp_path):
+def test_tp2_matches_single_gpu(kind, k, collective, tmp_path):
     ref = _run(_build(kind, k, torch.device("cuda", 0)), torch.device("cuda", 0))
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, kind, k, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, kind, k, port, str(tmp_path), collective))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
     got = torch.load(tmp_path / "tp.pt")
+    if isinstance(got, str):
+        pytest.skip("these GPUs have no NVLink multicast")
     for i, (a, b) in enumerate(zip(got, ref)):
         assert max_rel_err(a, b) < REL_TOL, i
