@@ -872,6 +872,7 @@ def sharded_40b_record(args, world, rank, device, dist_ok):
         torch.cuda.empty_cache()
         torch.distributed.barrier()
         tp = run_tp40b(sub, world, rank, device, True, quiet=True)
+    tp_error = collective_error(world, device)
     torch.cuda.empty_cache()
     cp = run_cp40b(sub, world, rank, device, dist_ok, quiet=True)
     torch.cuda.empty_cache()
@@ -889,7 +890,28 @@ def sharded_40b_record(args, world, rank, device, dist_ok):
            "tp": part(tp), "cp": part(cp)}
     rec["tp"]["decode_ms_per_step"] = tp["decode"]["ms_per_step"]
     rec["tp"]["decode_steps"] = tp["decode"]["steps"]
+    rec["tp"]["collective"] = tp["config"].get("collective")
+    if tp_error:
+        rec["tp"]["error"] = "a cross-rank wait of the in-switch all-reduce expired"
     return rec
+
+
+def collective_error(world, device) -> bool:
+    """True when an in-switch reducer of any rank reports an expired cross-rank
+    wait (agreed over the ranks, so that all take the same path)."""
+    from evo2_flash_b200 import parallel
+
+    err = 0
+    for red in parallel._REDUCERS.values():
+        if red:
+            red.stream.synchronize()
+            err |= int(red.error.item())
+            red.error.zero_()
+    if world > 1:
+        t = torch.tensor([err], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        err = int(t.item())
+    return bool(err)
 
 
 def release_reducers():
