@@ -40,7 +40,9 @@ __device__ __forceinline__ bool block_ok(long long b, const hyena_state_view& v)
   return b >= 0 && b < v.num_blocks;
 }
 
-template <int KIND, int K>
+// V16 (LI only, chosen by the launcher): the staged state moves in 16-byte
+// chunks; needs an odd row width and 16-byte-aligned blocks.
+template <int KIND, int K, bool V16 = false>
 __global__ void __launch_bounds__(DEC_THREADS)
 decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   pdl_entry();
@@ -79,11 +81,15 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   // the snapshot block) is put in flight now, into shared memory with
   // cp.async, and read after the short filter (see the staged path below).
   constexpr bool kIIR = KIND == HYENA_KIND_IIR;
-  __shared__ float stage_sm[kIIR ? DEC_THREADS / 32 : 1][kIIR ? 32 * (IIR_STAGE_MAXD + 1) : 1];
+  __shared__ __align__(16) float stage_sm[kIIR ? DEC_THREADS / 32 : 1]
+                                        [kIIR ? 32 * (IIR_STAGE_MAXD + 1) : 1];
   const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
   const bool src_ok = block_ok(src, A.inner_state);
   const long long Dst = A.inner_state.dim_stride;
   const bool staged = kIIR && A.inner_state.col_stride == 1 && Dst >= 16 && Dst <= IIR_STAGE_MAXD;
+  // odd row width (the stamp column makes 17): the shared-memory rows need no
+  // padding, so the run moves as 16-byte chunks
+  constexpr bool staged16 = V16;
   if constexpr (kIIR) {
     if (staged) {
       const int lane = threadIdx.x & 31;
@@ -92,15 +98,24 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
       const long long h0 = (long long)(h - lane);  // the warp's first channel
       const float* sp = static_cast<const float*>(A.inner_state.data) +
                         src * A.inner_state.block_stride + h0 * Dst;
-      for (int j = lane; j < 32 * D; j += 32) {
-        float* d = &w[(j / D) * pitch + j % D];
-        if (src_ok)
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
-                           static_cast<uint32_t>(__cvta_generic_to_shared(d))),
-                       "l"(sp + j)
-                       : "memory");
-        else
-          *d = 0.0f;
+      if (staged16) {  // 32 D floats = 8 D 16-byte chunks (h0 D is a multiple of 4)
+        for (int j = lane; j < 8 * D; j += 32) {
+          if (src_ok)
+            cp_async16(&w[4 * j], sp + 4 * j);
+          else
+            *reinterpret_cast<float4*>(&w[4 * j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      } else {
+        for (int j = lane; j < 32 * D; j += 32) {
+          float* d = &w[(j / D) * pitch + j % D];
+          if (src_ok)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                             static_cast<uint32_t>(__cvta_generic_to_shared(d))),
+                         "l"(sp + j)
+                         : "memory");
+          else
+            *d = 0.0f;
+        }
       }
       cp_async_commit();
     }
@@ -243,14 +258,23 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) s[q] = add_rn(mul_rn(s[q], pl[q]), u[p]);
           if (dok[p]) {
+            float* dp = st + dst[p] * A.inner_state.block_stride + h0 * D;
             __syncwarp();  // the previous snapshot's stores have read the buffer
 #pragma unroll
             for (int q = 0; q < 16; ++q) w[lane * pitch + q] = s[q];
-            __syncwarp();
-            float* dp = st + dst[p] * A.inner_state.block_stride + h0 * D;
-            for (int j = lane; j < run; j += 32) {
-              const int c = j % (int)D;
-              if (c < 16) dp[j] = w[(j / (int)D) * pitch + c];
+            if (staged16) {
+              // the columns past the 16 modes (the position stamp) keep the
+              // destination block's values: read them into the run first
+              for (int c = 16; c < (int)D; ++c) w[lane * pitch + c] = dp[(long long)lane * D + c];
+              __syncwarp();
+              for (int j = lane; j < 8 * (int)D; j += 32)
+                *reinterpret_cast<float4*>(dp + 4 * j) = *reinterpret_cast<const float4*>(&w[4 * j]);
+            } else {
+              __syncwarp();
+              for (int j = lane; j < run; j += 32) {
+                const int c = j % (int)D;
+                if (c < 16) dp[j] = w[(j / (int)D) * pitch + c];
+              }
             }
           }
           y[p] = modal_readout16(s, rs);
@@ -621,6 +645,99 @@ static bool fast_path_ok(const hyena_layer_params& P, const hyena_decode_args& A
          aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % 4 == 0;
 }
 
+// The short filter of one verify step for 4 channels, whose (x2, x1, v) triples
+// are 12 contiguous bf16 columns: window columns off, off + 1 of S0 block cin,
+// then the n verified rows of z, oldest first (short_tap per column, the
+// arithmetic of decode_kernel); x2 and u = bf16(x1 v) per position.  The S0
+// window of block cout becomes old columns off + 1 .. followed by the new rows,
+// column by column in ascending order, so that in place (cout == cin) each old
+// column is read before it is overwritten.  Every access moves 4 bf16 (8 bytes).
+template <int NQ>
+__device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const hyena_decode_args& A,
+                                             int h, int t0, int n, int off, long long cin,
+                                             long long cout, bool write_conv,
+                                             float (&x2v)[NQ][4], float (&uv)[NQ][4]) {
+  const int W0 = A.conv_state.cols;
+  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
+  const long long bs = A.conv_state.block_stride, cs = A.conv_state.col_stride;
+  const bf16* win = s0 + cin * bs + 3 * h;
+  const uint2* swv = reinterpret_cast<const uint2*>(static_cast<const bf16*>(P.short_w) + 9 * h);
+  uint2 swr[9];  // 36 taps: column j's three at 3j
+#pragma unroll
+  for (int i = 0; i < 9; ++i) swr[i] = __ldg(swv + i);
+  // tap e of the 36 (e known at compile time after unrolling: stays in registers)
+  auto tap = [&](int e) {
+    const uint32_t w = (e & 2) ? swr[e >> 2].y : swr[e >> 2].x;
+    return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+  };
+  float c0[12], c1[12];
+#pragma unroll
+  for (int i = 0; i < 12; i += 4) {
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+    if (off < W0) load_bf16x4(win + (long long)off * cs + i, a);
+    if (off + 1 < W0) load_bf16x4(win + (long long)(off + 1) * cs + i, b);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      c0[i + k] = a[k];
+      c1[i + k] = b[k];
+    }
+  }
+  const bf16* z = static_cast<const bf16*>(A.z);
+#pragma unroll
+  for (int p = 0; p < NQ; ++p) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) x2v[p][c] = uv[p][c] = 0.0f;
+    if (p < n) {
+      const uint2* zp = reinterpret_cast<const uint2*>(z + (long long)(t0 + p) * A.ldz + 3 * h);
+      float xz[12];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        const uint2 zw = zp[i];
+        const float2 a = __bfloat1622float2(as_bf162(zw.x));
+        const float2 b = __bfloat1622float2(as_bf162(zw.y));
+        xz[4 * i] = a.x; xz[4 * i + 1] = a.y; xz[4 * i + 2] = b.x; xz[4 * i + 3] = b.y;
+      }
+      float o[12];
+#pragma unroll
+      for (int j = 0; j < 12; ++j) {
+        o[j] = short_tap(c0[j], c1[j], xz[j], tap(3 * j), tap(3 * j + 1), tap(3 * j + 2));
+        c0[j] = c1[j];
+        c1[j] = xz[j];
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        x2v[p][c] = o[3 * c];
+        uv[p][c] = bf16r(o[3 * c + 1] * o[3 * c + 2]);
+      }
+    }
+  }
+  if (write_conv) {
+    bf16* wout = s0 + cout * bs + 3 * h;
+    const int val = W0 - n;  // columns kept from the old window
+#pragma unroll
+    for (int i = 0; i < DEC_MAXW0; ++i) {
+      if (i >= W0) break;
+      uint2 v[3] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
+      if (i < val) {
+        const int sc = off + 1 + i;
+        if (sc < W0) {
+          const uint2* sp = reinterpret_cast<const uint2*>(win + (long long)sc * cs);
+#pragma unroll
+          for (int k = 0; k < 3; ++k) v[k] = sp[k];
+        }
+      } else {  // the verified row i - val again (an L1 hit)
+        const uint2* zp =
+            reinterpret_cast<const uint2*>(z + (long long)(t0 + i - val) * A.ldz + 3 * h);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) v[k] = zp[k];
+      }
+      uint2* dp = reinterpret_cast<uint2*>(wout + (long long)i * cs);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) dp[k] = v[k];
+    }
+  }
+}
+
 // FIR verify (q <= VQ positions per request, speculative windows): one thread
 // per (request, 4 channels).  The short filter runs per column exactly as in
 // decode_kernel; the inner FIR streams the accepted snapshot once with 16-byte
@@ -665,7 +782,6 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
              !(A.skip_null_writes && dst[p] == A.null_block);
   }
   bf16* out = static_cast<bf16*>(A.out);
-  const bf16* z = static_cast<const bf16*>(A.z);
   if ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state)) {
     if (!block_ok(cin, A.conv_state) && threadIdx.x == 0)
       flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
@@ -732,59 +848,12 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
 #pragma unroll
     for (int t = 0; t < U; ++t) sv[t] = nx[t];
   }
-  // ---- short filter per column of the 4 channels' triples, window shift (after
-  // the stream, so that its values are not held in registers across it)
-  const int W0 = A.conv_state.cols;
-  bf16* s0 = static_cast<bf16*>(A.conv_state.data);
-  const bf16* sw = static_cast<const bf16*>(P.short_w);
+  // ---- short filter of the 4 channels' triples, window shift (after the
+  // stream, so that its values are not held in registers across it)
   const bool write_conv = block_ok(cout, A.conv_state) &&
                           !(A.skip_null_writes && cout == A.null_block);
   float x2v[VQ][4], uv[VQ][4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    float xs[3][VQ];
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int col = 3 * (h + c) + q;
-      const float w0 = ldbf(sw + col * 3), w1 = ldbf(sw + col * 3 + 1), w2 = ldbf(sw + col * 3 + 2);
-      const bf16* wp = s0 + cin * A.conv_state.block_stride + col;
-      float c0 = off < W0 ? ldbf(wp + (long long)off * A.conv_state.col_stride) : 0.0f;
-      float c1 = off + 1 < W0 ? ldbf(wp + (long long)(off + 1) * A.conv_state.col_stride) : 0.0f;
-      float xz[VQ];
-#pragma unroll
-      for (int p = 0; p < VQ; ++p) {
-        xz[p] = 0.0f;
-        xs[q][p] = 0.0f;
-        if (p < n) {
-          xz[p] = ldbf(z + (long long)(t0 + p) * A.ldz + col);
-          xs[q][p] = short_tap(c0, c1, xz[p], w0, w1, w2);
-          c0 = c1;
-          c1 = xz[p];
-        }
-      }
-      if (write_conv) {
-        // column i <- old column off+1+i (read just before: in place, ascending
-        // i only overwrites columns already read) or the new inputs
-        const int val = W0 - n;
-        bf16* dp = s0 + cout * A.conv_state.block_stride + col;
-        for (int i = 0; i < W0; ++i) {
-          float v;
-          if (i < val) {
-            const int sc = off + 1 + i;
-            v = sc < W0 ? ldbf(wp + (long long)sc * A.conv_state.col_stride) : 0.0f;
-          } else {
-            v = pick(xz, i - val);
-          }
-          dp[(long long)i * A.conv_state.col_stride] = __float2bfloat16_rn(v);
-        }
-      }
-    }
-#pragma unroll
-    for (int p = 0; p < VQ; ++p) {
-      x2v[p][c] = xs[0][p];
-      uv[p][c] = bf16r(xs[1][p] * xs[2][p]);
-    }
-  }
+  verify_gate4<VQ>(P, A, h, t0, n, off, cin, cout, write_conv, x2v, uv);
 
   // the verified tokens themselves: newest taps, and the tail of each snapshot
 #pragma unroll
@@ -835,6 +904,11 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
 static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
   if (P.kind != HYENA_KIND_FIR || A.q > VQ) return false;
   if (A.conv_state.dim_stride != 1) return false;
+  // the short filter reads 4 channels' triples (12 bf16) with 8-byte loads
+  if (!aligned_elems(A.z, A.ldz, 2, 8) || !aligned_elems(P.short_w, 0, 2, 8)) return false;
+  if (!aligned_elems(A.conv_state.data, A.conv_state.block_stride, 2, 8) ||
+      (A.conv_state.col_stride * 2) % 8 != 0)
+    return false;
   if (!aligned_elems(A.out, A.ldo, 2, 8)) return false;
   const hyena_state_view& s = A.inner_state;
   if (s.dim_stride != 1 || P.inner_w_stride_h != 1 || (P.inner_w_stride_k * 2) % 8 != 0) return false;
@@ -873,7 +947,15 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaS
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
   if (P.kind == HYENA_KIND_IIR) {
     if (P.K != 16) return fail(HYENA_ERR_UNSUPPORTED, "IIR decode supports modal order 16");
-    launch_kernel(decode_kernel<HYENA_KIND_IIR, 16>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
+    const hyena_state_view& s = A.inner_state;
+    const bool v16 = s.col_stride == 1 && s.dim_stride >= 16 && s.dim_stride <= IIR_STAGE_MAXD &&
+                     (s.dim_stride & 1) && (s.block_stride & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(s.data) & 15u) == 0;
+    if (v16)
+      launch_kernel(decode_kernel<HYENA_KIND_IIR, 16, true>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u,
+                    P, A);
+    else
+      launch_kernel(decode_kernel<HYENA_KIND_IIR, 16>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
   } else if (P.K == 128) {
     launch_kernel(decode_kernel<HYENA_KIND_FIR, 128>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u, P, A);
   } else if (P.K == 7) {
