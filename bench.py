@@ -289,6 +289,37 @@ def run_prefill(layers, x, meta, steps, warmup, dist_ok, device, gemm_timer):
     return ms, clk.summary()
 
 
+class LocalNumaAlloc:
+    """Restricts this process to the CPUs of the GPU's NUMA node while pinned
+    host buffers are allocated (their pages land on the node whose memory
+    controller the GPU's PCIe link hangs off), then restores the affinity.
+    No-op where sysfs does not say."""
+
+    def __init__(self, device):
+        self.saved = None
+        try:
+            pr = torch.cuda.get_device_properties(device)
+            bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            node = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text())
+            cpus = set()
+            for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+            self.cpus = cpus if node >= 0 else None
+        except (OSError, ValueError, AttributeError, RuntimeError):
+            self.cpus = None
+
+    def __enter__(self):
+        if self.cpus:
+            self.saved = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.cpus & self.saved or self.saved)
+        return self
+
+    def __exit__(self, *a):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+
+
 def run_e2e(layers, x_host, meta, steps, device):
     """Public-API end to end: every step copies the hidden states from pinned host
     memory to the device, runs the triple, and copies the last layer's output
@@ -301,7 +332,8 @@ def run_e2e(layers, x_host, meta, steps, device):
     comp = torch.cuda.current_stream()
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
     xbuf = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
-    out_host = [torch.empty_like(x_host, pin_memory=True) for _ in range(2)]
+    with LocalNumaAlloc(device):
+        out_host = [torch.empty_like(x_host, pin_memory=True).fill_(0) for _ in range(2)]
     uploaded = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(2)]
     torch.cuda.synchronize()
@@ -1085,7 +1117,8 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        x_host = x.cpu().pin_memory()
+        with LocalNumaAlloc(device):
+            x_host = x.cpu().pin_memory()
         e_steps = max(3, args.steps)
         e_ms, h2d, d2h = run_e2e(layers, x_host, meta, e_steps, device)
         e_step = e_ms / e_steps
@@ -1104,7 +1137,7 @@ def main():
                          f"in_proj as bf16 GEMM on dequantised e4m3 weights), median of 3"}
 
     model7b = None
-    if rank == 0 and world == 1 and not args.no_model7b:
+    if rank == 0 and world == 1 and not args.no_model7b and args.only is None:
         ml = run_model7b(args, device, quiet=True)
         model7b = {"workload": ml["config"]["workload"], "tok_per_s": ml["value"],
                    "mean_nll": ml["mean_nll"], "ms": ml["ms_per_step"],
@@ -1112,7 +1145,7 @@ def main():
         torch.cuda.empty_cache()
 
     sharded = None
-    if not args.no_40b:
+    if not args.no_40b and args.only is None:
         del layers
         torch.cuda.empty_cache()
         sharded = sharded_40b_record(args, world, rank, device, dist_ok)

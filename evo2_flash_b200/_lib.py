@@ -13,7 +13,7 @@ from ._build import LIB_PATH
 
 HYENA_KIND_FIR = 0
 HYENA_KIND_IIR = 1
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 class StateView(C.Structure):
@@ -96,6 +96,8 @@ class DecodeArgs(C.Structure):
         ("conv_state", StateView),
         ("inner_state", StateView),
         ("error_flags", C.c_void_p),
+        ("conv_in_stride", C.c_int64),
+        ("conv_out_stride", C.c_int64),
     ]
 
 

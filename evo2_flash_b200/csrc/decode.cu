@@ -63,10 +63,14 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
     n = min(A.q, DEC_MAXQ);
   }
-  const int accepted = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+  int accepted = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+  if (accepted > A.q) {  // past the slot table's columns
+    if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+    accepted = A.q;
+  }
   const int off = accepted - 1;
-  const long long cin = __ldg(A.conv_in_block + r);
-  const long long cout = __ldg(A.conv_out_block + r);
+  const long long cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+  const long long cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
   bf16* out = static_cast<bf16*>(A.out);
   const bf16* z = static_cast<const bf16*>(A.z);
 
@@ -231,10 +235,22 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
     }
   } else {
     float s[16], pl[16], rs[16];
+    if constexpr (V16) {  // contiguous, 16-byte-aligned rows (checked by the launcher)
+      const float4* lp4 = reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h);
+      const float4* rs4 = reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h);
 #pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      pl[q] = expf(P.log_poles[(long long)h * P.lp_stride_h + q * P.lp_stride_s]);
-      rs[q] = P.residues[(long long)h * P.res_stride_h + q * P.res_stride_s];
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 a = __ldg(lp4 + q4), b = __ldg(rs4 + q4);
+        pl[4 * q4] = expf(a.x); pl[4 * q4 + 1] = expf(a.y);
+        pl[4 * q4 + 2] = expf(a.z); pl[4 * q4 + 3] = expf(a.w);
+        rs[4 * q4] = b.x; rs[4 * q4 + 1] = b.y; rs[4 * q4 + 2] = b.z; rs[4 * q4 + 3] = b.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        pl[q] = expf(P.log_poles[(long long)h * P.lp_stride_h + q * P.lp_stride_s]);
+        rs[q] = P.residues[(long long)h * P.res_stride_h + q * P.res_stride_s];
+      }
     }
     // Modes contiguous (S2 rows of D >= 16 floats, the stamp column included):
     // a warp's 32 channels are one contiguous run of 32 D floats per block, so
@@ -416,8 +432,8 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
   if (h >= P.H) return;
   // Routing first, all four loads in flight at once.
-  const long long cin = __ldg(A.conv_in_block + r);
-  const long long cout = __ldg(A.conv_out_block + r);
+  const long long cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+  const long long cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
   const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0);
   const long long dst = __ldg(A.out_slots + (long long)r * A.out_stride0);
   bf16* out = static_cast<bf16*>(A.out) + (long long)r * A.ldo + h;
@@ -502,6 +518,29 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 // thread 0.
 constexpr int IIR_R = 8;
 constexpr int IIR_CH = 64;
+
+// modal_readout16 over a channel's 16 modes held by four consecutive lanes
+// (lane t of the quad owns modes 4t .. 4t+3): the same halving tree, modes s
+// and s + 8 meeting across lanes t and t^2, s and s + 4 across t and t^1, the
+// rest inside lane 0 of the quad, which alone returns the readout.  Called by
+// all 32 lanes of the warp.
+__device__ __forceinline__ float quad_readout(const float (&s4)[4], const float (&res)[4]) {
+  const unsigned full = 0xffffffffu;
+  float q[4], o[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) q[m] = mul_rn(s4[m], res[m]);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 2);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 8] (t < 2)
+#pragma unroll
+  for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 1);
+#pragma unroll
+  for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 4] (t == 0)
+  q[0] = add_rn(q[0], q[2]);
+  q[1] = add_rn(q[1], q[3]);
+  return add_rn(q[0], q[1]);
+}
 constexpr int IIR_THREADS = 256;
 static_assert(IIR_R * IIR_CH / 4 <= IIR_THREADS, "one gate item per thread");
 
@@ -516,13 +555,12 @@ decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   const int hb = blockIdx.x * IIR_CH;
   const int h = hb + cl;     // H % 64 == 0: always a valid channel
   const int r0 = blockIdx.y * IIR_R;
-  const unsigned full = 0xffffffffu;
   if (threadIdx.x < 4 * IIR_R) {
     const int i = threadIdx.x % IIR_R, f = threadIdx.x / IIR_R, r = r0 + i;
     long long v = -1;
     if (r < A.num_reqs) {
-      if (f == 0) v = __ldg(A.conv_in_block + r);
-      else if (f == 1) v = __ldg(A.conv_out_block + r);
+      if (f == 0) v = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+      else if (f == 1) v = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
       else if (f == 2) v = __ldg(A.in_slots + (long long)r * A.in_stride0);
       else v = __ldg(A.out_slots + (long long)r * A.out_stride0);
     }
@@ -596,21 +634,9 @@ decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
       *reinterpret_cast<float4*>(st + route[3][i] * A.inner_state.block_stride +
                                  (long long)h * A.inner_state.dim_stride + 4 * t) =
           make_float4(s4[0], s4[1], s4[2], s4[3]);
-    float q[4], o[4];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) q[m] = mul_rn(s4[m], res[m]);
-#pragma unroll
-    for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 2);
-#pragma unroll
-    for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 8] (t < 2)
-#pragma unroll
-    for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 1);
+    const float yr = quad_readout(s4, res);
     if (t == 0) {
-#pragma unroll
-      for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 4]
-      q[0] = add_rn(q[0], q[2]);
-      q[1] = add_rn(q[1], q[3]);
-      float y = bf16r(add_rn(q[0], q[1]));
+      float y = bf16r(yr);
       if (Dg) y = bf16r(y + bf16r(dval * u));
       outp[orow + h] = __float2bfloat16_rn(bf16r(x2 * y));
     }
@@ -768,10 +794,14 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
     if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
     n = min(A.q, VQ);
   }
-  const int accepted = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+  int accepted = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+  if (accepted > A.q) {  // past the slot table's columns
+    if (threadIdx.x == 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+    accepted = A.q;
+  }
   const int off = accepted - 1;
-  const long long cin = __ldg(A.conv_in_block + r);
-  const long long cout = __ldg(A.conv_out_block + r);
+  const long long cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+  const long long cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
   const long long src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
   long long dst[VQ];
   bool dok[VQ];
@@ -900,16 +930,21 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
   }
 }
 
-// The FIR verify path: up to VQ positions, unit channel strides, 16-byte rows.
-static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
-  if (P.kind != HYENA_KIND_FIR || A.q > VQ) return false;
-  if (A.conv_state.dim_stride != 1) return false;
-  // the short filter reads 4 channels' triples (12 bf16) with 8-byte loads
+// verify_gate4 and the 4-channel output stores: 8-byte accesses to z, the
+// short taps, the S0 window (unit channel stride) and out, and to D.
+static bool gate4_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
+  if (A.q > VQ || A.conv_state.dim_stride != 1) return false;
   if (!aligned_elems(A.z, A.ldz, 2, 8) || !aligned_elems(P.short_w, 0, 2, 8)) return false;
   if (!aligned_elems(A.conv_state.data, A.conv_state.block_stride, 2, 8) ||
       (A.conv_state.col_stride * 2) % 8 != 0)
     return false;
-  if (!aligned_elems(A.out, A.ldo, 2, 8)) return false;
+  if (P.D && !aligned_elems(P.D, 0, 2, 8)) return false;
+  return aligned_elems(A.out, A.ldo, 2, 8) && P.H % 4 == 0;
+}
+
+// The FIR verify path: up to VQ positions, unit channel strides, 16-byte rows.
+static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
+  if (P.kind != HYENA_KIND_FIR || !gate4_ok(P, A)) return false;
   const hyena_state_view& s = A.inner_state;
   if (s.dim_stride != 1 || P.inner_w_stride_h != 1 || (P.inner_w_stride_k * 2) % 8 != 0) return false;
   if (!aligned_elems(P.inner_w, 0, 2, 8) || (P.D && !aligned_elems(P.D, 0, 2, 8))) return false;
@@ -917,7 +952,216 @@ static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& 
          P.H % 4 == 0;
 }
 
-int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaStream_t st) {
+// LI verify (q <= VQ positions per request, speculative windows, S2 rows of
+// D = 16 .. 20 floats: the 16 modes, then padding columns, the last of channel
+// 0 holding the block's position stamp).  A block covers 64 channels of LV_R
+// requests, whose rows form one contiguous, 16-byte-aligned run of 64 D floats
+// per state block:
+//   1. every request's source run is put in flight into shared memory (16-byte
+//      cp.async) before anything else;
+//   2. one thread per (request, 4 channels) runs the short filter
+//      (verify_gate4), x2 and u to shared memory;
+//   3. four threads per channel, four modes each (the quad layout of
+//      decode_iir_q1_kernel), advance the state position by position: each
+//      snapshot is written over the modes of the run in shared memory and every
+//      warp stores its 8 channels' rows (8 D floats) with 16-byte stores.  The
+//      padding columns so travel from the source block, except channel 0's
+//      (the stamp), which are never written;
+//   4. the (request, 4 channels) threads apply D and the x2 gate, 8-byte stores.
+// Same arithmetic, order and rounding as decode_kernel.
+constexpr int LV_R = 4;
+constexpr int LV_CH = 64;
+constexpr int LV_THREADS = 256;
+static_assert(LV_R * LV_CH / 4 <= LV_THREADS, "one gate item per thread");
+
+__global__ void __launch_bounds__(LV_THREADS, 2)
+decode_iir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) {
+  __shared__ __align__(16) float run_sm[LV_R][LV_CH * IIR_STAGE_MAXD];
+  __shared__ float u_s[LV_R][VQ][LV_CH], x2_s[LV_R][VQ][LV_CH], y_s[LV_R][VQ][LV_CH];
+  __shared__ long long rt_cin[LV_R], rt_cout[LV_R], rt_src[LV_R], rt_dst[LV_R][VQ];
+  __shared__ int rt_t0[LV_R], rt_n[LV_R], rt_off[LV_R], rt_flags[LV_R];
+  constexpr int F_ZERO = 1, F_SRC = 2, F_CONV = 4;  // rt_flags bits; dst p ok: bit 8 + p
+  pdl_entry();
+  const int hb = blockIdx.x * LV_CH, r0 = blockIdx.y * LV_R;
+  const int D = (int)A.inner_state.dim_stride;
+  const long long bs = A.inner_state.block_stride;
+  float* st = static_cast<float*>(A.inner_state.data);
+  if (threadIdx.x < LV_R) {
+    const int i = threadIdx.x, r = r0 + i;
+    int t0 = 0, n = 0, off = 0, fl = 0;
+    long long cin = -1, cout = -1, src = -1;
+    if (r < A.num_reqs) {
+      if (A.token_start) {
+        t0 = __ldg(A.token_start + r);
+        n = __ldg(A.token_start + r + 1) - t0;
+      } else {
+        t0 = r;
+        n = 1;
+      }
+      if (n > A.q || n > VQ) {
+        flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+        n = min(A.q, VQ);
+      }
+      n = max(n, 0);
+    }
+    if (n > 0) {
+      int acc = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+      if (acc > A.q) {  // past the slot table's columns
+        flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+        acc = A.q;
+      }
+      off = acc - 1;
+      cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+      cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
+      src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
+      const bool cin_ok = block_ok(cin, A.conv_state);
+      if ((A.zero_null_rows && cin == A.null_block) || !cin_ok) fl |= F_ZERO;
+      if (block_ok(src, A.inner_state)) fl |= F_SRC;
+      if (block_ok(cout, A.conv_state) && !(A.skip_null_writes && cout == A.null_block))
+        fl |= F_CONV;
+      if (!cin_ok || (!(fl & F_ZERO) && !(fl & F_SRC)))
+        flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+#pragma unroll
+      for (int p = 0; p < VQ; ++p) {
+        long long d = -1;
+        if (p < n) {
+          d = __ldg(A.out_slots + (long long)r * A.out_stride0 + (long long)p * A.out_stride1);
+          if (!(fl & F_ZERO) && block_ok(d, A.inner_state) &&
+              !(A.skip_null_writes && d == A.null_block))
+            fl |= 256 << p;
+        }
+        rt_dst[i][p] = d;
+      }
+    }
+    rt_t0[i] = t0;
+    rt_n[i] = n;
+    rt_off[i] = off;
+    rt_flags[i] = fl;
+    rt_cin[i] = cin;
+    rt_cout[i] = cout;
+    rt_src[i] = src;
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int t = lane & 3;                 // modes 4t .. 4t+3
+  const int cl = warp * 8 + (lane >> 2);  // channel within the block
+  const float4 lp4 = __ldg(reinterpret_cast<const float4*>(P.log_poles + (long long)(hb + cl) * P.lp_stride_h) + t);
+  const float4 rs4 = __ldg(reinterpret_cast<const float4*>(P.residues + (long long)(hb + cl) * P.res_stride_h) + t);
+  __syncthreads();
+
+  // 1. source runs: 16 D chunks of 16 bytes per request
+  const int chunks = 16 * D;
+  for (int j = threadIdx.x; j < LV_R * chunks; j += LV_THREADS) {
+    const int i = j / chunks, c = j - i * chunks;
+    if (rt_n[i] == 0 || (rt_flags[i] & F_ZERO)) continue;
+    float* d = &run_sm[i][4 * c];
+    if (rt_flags[i] & F_SRC)
+      cp_async16(d, st + rt_src[i] * bs + (long long)hb * D + 4 * c);
+    else
+      *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  cp_async_commit();
+
+  // 2. short filter + gate, item = (request i, channels 4 c4 .. 4 c4 + 3)
+  const int gi = threadIdx.x / (LV_CH / 4), gc = threadIdx.x % (LV_CH / 4);
+  const bool gate_item = threadIdx.x < LV_R * LV_CH / 4;
+  if (gate_item && rt_n[gi] > 0 && !(rt_flags[gi] & F_ZERO)) {
+    float x2v[VQ][4], uv[VQ][4];
+    verify_gate4<VQ>(P, A, hb + 4 * gc, rt_t0[gi], rt_n[gi], rt_off[gi], rt_cin[gi], rt_cout[gi],
+                     (rt_flags[gi] & F_CONV) != 0, x2v, uv);
+#pragma unroll
+    for (int p = 0; p < VQ; ++p)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        x2_s[gi][p][4 * gc + c] = x2v[p][c];
+        u_s[gi][p][4 * gc + c] = uv[p][c];
+      }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // 3. modal recurrence, snapshots, readout
+  const float pole[4] = {expf(lp4.x), expf(lp4.y), expf(lp4.z), expf(lp4.w)};
+  const float res[4] = {rs4.x, rs4.y, rs4.z, rs4.w};
+  const bool stamp_rows = D > 16 && hb == 0 && warp == 0;  // chunk 4 holds channel 0's columns 16..
+#pragma unroll 1
+  for (int i = 0; i < LV_R; ++i) {
+    const int n = rt_n[i], fl = rt_flags[i];
+    if (n == 0 || (fl & F_ZERO)) continue;  // uniform
+    float* runp = run_sm[i];
+    float s4[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) s4[m] = runp[cl * D + 4 * t + m];
+#pragma unroll
+    for (int p = 0; p < VQ; ++p) {
+      if (p >= n) break;  // uniform
+      const float u = u_s[i][p][cl];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) s4[m] = add_rn(mul_rn(s4[m], pole[m]), u);
+      if (fl & (256 << p)) {  // uniform
+        __syncwarp();  // the previous snapshot's stores have read the run
+#pragma unroll
+        for (int m = 0; m < 4; ++m) runp[cl * D + 4 * t + m] = s4[m];
+        __syncwarp();
+        const float* sp = runp + 8 * warp * D;
+        float* dp = st + rt_dst[i][p] * bs + (long long)(hb + 8 * warp) * D;
+        for (int j = lane; j < 2 * D; j += 32) {
+          const float4 v = *reinterpret_cast<const float4*>(sp + 4 * j);
+          if (stamp_rows && j == 4) {
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (16 + k >= D) dp[16 + k] = e[k];
+          } else {
+            *reinterpret_cast<float4*>(dp + 4 * j) = v;
+          }
+        }
+      }
+      const float yr = quad_readout(s4, res);
+      if (t == 0) y_s[i][p][cl] = yr;
+    }
+  }
+  __syncthreads();
+
+  // 4. output gate
+  if (gate_item && rt_n[gi] > 0) {
+    const int n = rt_n[gi], t0 = rt_t0[gi];
+    bf16* out = static_cast<bf16*>(A.out) + hb + 4 * gc;
+    if (rt_flags[gi] & F_ZERO) {
+      const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int p = 0; p < n; ++p) store_bf16x4(out + (long long)(t0 + p) * A.ldo, zero);
+    } else {
+      const bf16* Dg = static_cast<const bf16*>(P.D);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if (Dg) load_bf16x4(Dg + hb + 4 * gc, d);
+      for (int p = 0; p < n; ++p) {
+        float g[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float yy = bf16r(y_s[gi][p][4 * gc + c]);
+          if (Dg) yy = bf16r(yy + bf16r(d[c] * u_s[gi][p][4 * gc + c]));
+          g[c] = bf16r(x2_s[gi][p][4 * gc + c] * yy);
+        }
+        store_bf16x4(out + (long long)(t0 + p) * A.ldo, g);
+      }
+    }
+  }
+}
+
+// The LI verify path: gate4_ok, S2 rows of 16 .. 20 contiguous floats in
+// 16-byte-aligned blocks, poles / residues rows as 16-byte vectors.
+static bool iir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& A) {
+  if (P.kind != HYENA_KIND_IIR || P.K != 16 || !gate4_ok(P, A)) return false;
+  const hyena_state_view& s = A.inner_state;
+  return s.col_stride == 1 && s.dim_stride >= 16 && s.dim_stride <= IIR_STAGE_MAXD &&
+         aligned_elems(s.data, s.block_stride, 4, 16) && P.lp_stride_s == 1 &&
+         P.res_stride_s == 1 && aligned_elems(P.log_poles, P.lp_stride_h, 4, 16) &&
+         aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % LV_CH == 0;
+}
+
+int decode_launch(const hyena_layer_params& P, const hyena_decode_args& args, cudaStream_t st) {
+  hyena_decode_args A = args;
+  if (A.conv_in_stride == 0) A.conv_in_stride = 1;
+  if (A.conv_out_stride == 0) A.conv_out_stride = 1;
   if (A.conv_state.cols > DEC_MAXW0)
     return fail(HYENA_ERR_UNSUPPORTED, "conv window wider than 8 columns");
   if (fast_path_ok(P, A)) {
@@ -944,13 +1188,20 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& A, cudaS
       launch_kernel(decode_fir_verify_kernel<7>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
     return check_launch("decode_fir_verify_kernel");
   }
+  if (iir_verify_ok(P, A)) {
+    dim3 g(P.H / LV_CH, (A.num_reqs + LV_R - 1) / LV_R);
+    launch_kernel(decode_iir_verify_kernel, dim3(g), dim3(LV_THREADS), 0, st, 0u, P, A);
+    return check_launch("decode_iir_verify_kernel");
+  }
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
   if (P.kind == HYENA_KIND_IIR) {
     if (P.K != 16) return fail(HYENA_ERR_UNSUPPORTED, "IIR decode supports modal order 16");
     const hyena_state_view& s = A.inner_state;
     const bool v16 = s.col_stride == 1 && s.dim_stride >= 16 && s.dim_stride <= IIR_STAGE_MAXD &&
                      (s.dim_stride & 1) && (s.block_stride & 3) == 0 &&
-                     (reinterpret_cast<uintptr_t>(s.data) & 15u) == 0;
+                     (reinterpret_cast<uintptr_t>(s.data) & 15u) == 0 && P.lp_stride_s == 1 &&
+                     P.res_stride_s == 1 && aligned_elems(P.log_poles, P.lp_stride_h, 4, 16) &&
+                     aligned_elems(P.residues, P.res_stride_h, 4, 16);
     if (v16)
       launch_kernel(decode_kernel<HYENA_KIND_IIR, 16, true>, dim3(grid), dim3(DEC_THREADS), 0, st, 0u,
                     P, A);

@@ -49,7 +49,9 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024 / STAGE_BYTES) > 8 ? 8 : (192 * 1024 / STAGE_BYTES);
-  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
+  // two accumulators, allocated as a power of two >= 32 columns (BN = 192: 512)
+  static constexpr uint32_t TMEM_COLS =
+      2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
 };
 
 template <int BN>
@@ -843,8 +845,11 @@ static int resident(int bn, int splits) {
   }
 }
 
-// Large M: the widest N-tile that still gives every SM a tile (persistent
-// kernel, splits = 0).  Small M (decode batches): the cluster kernel with the
+// Large M: the persistent kernel (splits = 0) with the N-tile width that gives
+// every SM a tile and the shortest last wave: cost = waves x (BN + 32), the 32
+// standing for a tile's fixed epilogue share; 256 unless another width is at
+// least 10% cheaper (M = 512 x N = 12288: 192-wide tiles, 256 tiles in 2 waves
+// instead of 192 tiles whose second wave is nearly as long as the first).  Small M (decode batches): the cluster kernel with the
 // (BN, splits) that, in one resident wave of at most one CTA per SM, puts the
 // fewest operand bytes through any one SM ((BM + BN) x its K slice; ties: fewer
 // splits), each K slice at least two stages long.
@@ -852,8 +857,21 @@ template <bool FP8>
 static Plan plan(int M, int N, int K) {
   const long long mt = (M + BM - 1) / BM;
   const int sms = num_sms();
-  for (int bn : {256, 128}) {
-    if (mt * ((N + bn - 1) / bn) >= sms) return {bn, 0};
+  {
+    int pick = 0;
+    long long pick_cost = 0, cost256 = -1;
+    for (int bn : {256, 192, 128}) {
+      const long long tiles = mt * ((N + bn - 1) / bn);
+      if (tiles < sms) continue;
+      const long long cost = ((tiles + sms - 1) / sms) * (bn + 32);
+      if (bn == 256) cost256 = cost;
+      if (pick == 0 || cost < pick_cost) {
+        pick = bn;
+        pick_cost = cost;
+      }
+    }
+    if (pick != 0 && cost256 >= 0 && pick != 256 && 10 * pick_cost > 9 * cost256) pick = 256;
+    if (pick != 0) return {pick, 0};
   }
   const int kblocks = K / (BKB / (FP8 ? 1 : 2));
   Plan best = {0, 0};
@@ -906,6 +924,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   }
   switch (pl.bn) {
     case 256: return launch_bn<FP8, 256>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
+    case 192: return launch_bn<FP8, 192>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
     case 128: return launch_bn<FP8, 128>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
     case 64: return launch_bn<FP8, 64>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
     default: return launch_bn<FP8, 32>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);

@@ -116,8 +116,9 @@ class DecodePlan:
     out_slots (reqs, q) blocks the state after token p is written to
     starts    (reqs + 1,) token offsets of the requests, or None (one each)
     conv_in / conv_out  (reqs,) blocks of the short-filter window
-    engine_accepted     the engine's own accepted counts (>= 1), or None when
-                        it sent none (the kernels then read every count as 1)
+    engine_accepted     the engine's own accepted counts (the kernels read a
+                        count below 1 as 1), or None when it sent none (every
+                        count then reads as 1)
     """
 
     reqs: int
@@ -179,7 +180,7 @@ def plan_decode(m, positions, num_blocks):
         if engine.numel() < reqs:
             raise ValueError(f"num_accepted_tokens holds {engine.numel()} counts for "
                              f"{reqs} requests")
-        engine = engine[:reqs].clamp_min(1)
+        engine = engine[:reqs]  # counts below 1 read as 1 in the kernels
     width = min(table.shape[1], positions)
     prev = getattr(m, "block_idx_last_scheduled_token_prev_step", None)
     sched = getattr(m, "block_idx_last_scheduled_token", None)

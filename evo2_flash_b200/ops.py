@@ -189,7 +189,7 @@ def decode(w: LayerWeights, z, out, conv_in_block, conv_out_block, in_slots, out
 
     conv_in_block / conv_out_block (B,) int; in_slots / out_slots (B, q) int
     (q = 1 for ordinary decode); token_start (B+1,) int or None (one token per
-    request); accepted (B,) int >= 1 or None.
+    request); accepted (B,) int (a count below 1 reads as 1) or None.
     """
     B = conv_in_block.shape[0]
     _require(z.dim() == 2 and z.shape[1] == 3 * w.H and z.dtype == BF16 and z.stride(1) == 1,
@@ -203,8 +203,12 @@ def decode(w: LayerWeights, z, out, conv_in_block, conv_out_block, in_slots, out
     _require(1 <= q <= 8, f"at most 8 positions per request, got {q}")
     if B == 0:
         return out
-    cin = _i32(conv_in_block, "conv_in_block").contiguous()
-    cout = _i32(conv_out_block, "conv_out_block").contiguous()
+    cin = _i32(conv_in_block, "conv_in_block")
+    cout = _i32(conv_out_block, "conv_out_block")
+    if cin.dim() != 1 or cin.stride(0) < 1:
+        cin = cin.contiguous().view(-1)
+    if cout.dim() != 1 or cout.stride(0) < 1:
+        cout = cout.contiguous().view(-1)
     ins = _i32(in_slots, "in_slots")
     outs = _i32(out_slots, "out_slots")
     ts = None if token_start is None else _i32(token_start[: B + 1], "token_start").contiguous()
@@ -216,6 +220,7 @@ def decode(w: LayerWeights, z, out, conv_in_block, conv_out_block, in_slots, out
     a.token_start = None if ts is None else ts.data_ptr()
     a.accepted = None if acc is None else acc.data_ptr()
     a.conv_in_block, a.conv_out_block = cin.data_ptr(), cout.data_ptr()
+    a.conv_in_stride, a.conv_out_stride = cin.stride(0), cout.stride(0)
     a.in_slots, a.in_stride0, a.in_stride1 = ins.data_ptr(), ins.stride(0), ins.stride(1)
     a.out_slots, a.out_stride0, a.out_stride1 = outs.data_ptr(), outs.stride(0), outs.stride(1)
     a.zero_null_rows = int(bool(zero_null_rows))

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define HYENA_ABI_VERSION 7
+#define HYENA_ABI_VERSION 8
 
 #if defined(__GNUC__)
 #define HYENA_API __attribute__((visibility("default")))
@@ -171,8 +171,9 @@ typedef struct hyena_decode_args {
   int32_t num_reqs;
   int32_t q;                    /* max tokens per request (columns of in/out slots) */
   const int32_t* token_start;   /* (num_reqs + 1) or NULL */
-  const int32_t* accepted;      /* (num_reqs) >= 1, or NULL */
-  const int32_t* conv_in_block; const int32_t* conv_out_block;  /* (num_reqs) */
+  const int32_t* accepted;      /* (num_reqs), read clamped to [1, q] (above q also sets
+                                   HYENA_FLAG_SEGMENT); or NULL (= 1) */
+  const int32_t* conv_in_block; const int32_t* conv_out_block;  /* (num_reqs), strided below */
   const int32_t* in_slots; int64_t in_stride0, in_stride1;      /* (num_reqs, q) */
   const int32_t* out_slots; int64_t out_stride0, out_stride1;   /* (num_reqs, q) */
   int32_t zero_null_rows;
@@ -181,6 +182,8 @@ typedef struct hyena_decode_args {
   hyena_state_view conv_state;
   hyena_state_view inner_state;
   int32_t* error_flags;
+  int64_t conv_in_stride;       /* elements between consecutive conv_in_block entries */
+  int64_t conv_out_stride;      /* ... conv_out_block entries; 0 reads as 1 (contiguous) */
 } hyena_decode_args;
 
 HYENA_API int hyena_decode(const hyena_layer_params* p, const hyena_decode_args* a, void* stream);

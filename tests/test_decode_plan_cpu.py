@@ -37,7 +37,7 @@ def test_speculative_table_and_engine_counts():
     p = plan_decode(_meta(t, 6, starts, num_accepted_tokens=acc), 4, 64)
     assert p.in_slots.tolist() == [[1, 2, 3, 4], [5, 6, 7, 8]]  # width = positions
     assert p.starts.tolist() == [0, 4, 6]
-    assert p.engine_accepted.tolist() == [1, 3]  # clamped to >= 1, cut to the requests
+    assert p.engine_accepted.tolist() == [0, 3]  # cut to the requests (kernels read 0 as 1)
     assert p.conv_in.tolist() == [1, 5]
 
 

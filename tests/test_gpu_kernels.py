@@ -185,6 +185,48 @@ def test_verify_matches_oracle(kind, k):
         assert torch.equal(ds[1].cpu()[1:, : k - 1], ref_states[1][1:, : k - 1])
 
 
+@pytest.mark.parametrize("kind,k", KINDS)
+def test_verify_many_requests_matches_oracle(kind, k):
+    """Speculative verify over several channel and request groups of every
+    kernel: 19 requests with ragged lengths 1..4 and accepted counts 1..4 on
+    scrambled verifier slots (the accepted snapshot is often also a slot the
+    step writes).  The position stamps (channel 0's last S2 column) stay as
+    they were: only hyena_spec_record writes them."""
+    from evo2_flash_b200 import ops
+
+    H, B, q = 512, 19, 4
+    p = random_params(kind, H, k, seed=44)
+    po = params_to_oracle(p, kind, H, k)
+    g = torch.Generator().manual_seed(45)
+    nb = 1 + B * q
+    order = (torch.randperm(nb - 1, generator=g) + 1).view(B, q)
+    slots = order.tolist()
+    lengths = torch.randint(1, q + 1, (B,), generator=g).tolist()
+    accepted = torch.randint(1, q + 1, (B,), generator=g)
+    states = _random_states(H, nb, 2 + q - 1, seed=46, spec_col=True)
+    ref_states = [s.clone() for s in states]
+    T = sum(lengths)
+    z = (torch.randn(T, 3 * H, generator=g) * 0.5).to(torch.bfloat16)
+    meta = decode_meta(slots, lengths, computed=[100 + r for r in range(B)])
+    ref = O.mixer_core(z, po, meta, ref_states, accepted, bf16_products=True)
+    w = _weights({kk: v.to(DEV) for kk, v in p.items()}, kind)
+    ds = [s.to(DEV) for s in states]
+    stamps_before = ds[2][:, 0, 16].clone()
+    st = torch.tensor(slots, dtype=torch.int32, device=DEV)
+    qs = meta.query_start_loc_d.to(DEV)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=DEV)
+    ops.decode(w, z.to(DEV), out, st[:, 0], st[:, 0], st, st, ds[0],
+               ds[2] if kind == "hcl" else ds[1], token_start=qs, accepted=accepted.to(DEV))
+    torch.cuda.synchronize()
+    assert max_rel_err(out.cpu(), ref) < REL_TOL
+    assert torch.equal(ds[0].cpu()[1:], ref_states[0][1:])
+    if kind == "hcl":
+        assert max_rel_err(ds[2].cpu()[1:, :, :16], ref_states[2][1:, :, :16]) < 1e-5
+        assert torch.equal(ds[2][:, 0, 16], stamps_before)
+    else:
+        assert torch.equal(ds[1].cpu()[1:, : k - 1], ref_states[1][1:, : k - 1])
+
+
 @pytest.mark.parametrize("kind,k", [("hcm", 128), ("hcl", 16)])
 def test_decode_null_block_row_is_zero_and_writes_nothing(kind, k):
     from evo2_flash_b200 import ops
@@ -416,8 +458,9 @@ def test_rms_norm_rejects_bad_arguments():
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
                                    (4096, 12288, 4096), (128, 12288, 4096), (1024, 4096, 4096),
-                                   (7, 4096, 256)])
+                                   (7, 4096, 256), (512, 12288, 4096), (500, 12288, 1024)])
 def test_gemm_e4m3(M, N, K):
+    """(512 | 500, 12288): 192-wide persistent tiles (the q = 4 verify in_proj)."""
     from evo2_flash_b200 import ops
 
     g = torch.Generator().manual_seed(M + N)
