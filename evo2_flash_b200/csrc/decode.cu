@@ -738,28 +738,37 @@ __device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const 
     }
   }
   if (write_conv) {
+    // every value of the new window is loaded before the first store, so the
+    // loads overlap and, in place, each old column is read before it is
+    // overwritten
     bf16* wout = s0 + cout * bs + 3 * h;
     const int val = W0 - n;  // columns kept from the old window
+    uint2 v[DEC_MAXW0][3];
 #pragma unroll
     for (int i = 0; i < DEC_MAXW0; ++i) {
-      if (i >= W0) break;
-      uint2 v[3] = {make_uint2(0u, 0u), make_uint2(0u, 0u), make_uint2(0u, 0u)};
-      if (i < val) {
-        const int sc = off + 1 + i;
-        if (sc < W0) {
-          const uint2* sp = reinterpret_cast<const uint2*>(win + (long long)sc * cs);
 #pragma unroll
-          for (int k = 0; k < 3; ++k) v[k] = sp[k];
+      for (int k = 0; k < 3; ++k) v[i][k] = make_uint2(0u, 0u);
+      if (i < W0) {
+        const uint2* sp = nullptr;
+        if (i < val) {
+          const int sc = off + 1 + i;
+          if (sc < W0) sp = reinterpret_cast<const uint2*>(win + (long long)sc * cs);
+        } else {  // the verified row i - val again (an L1 hit)
+          sp = reinterpret_cast<const uint2*>(z + (long long)(t0 + i - val) * A.ldz + 3 * h);
         }
-      } else {  // the verified row i - val again (an L1 hit)
-        const uint2* zp =
-            reinterpret_cast<const uint2*>(z + (long long)(t0 + i - val) * A.ldz + 3 * h);
+        if (sp) {
 #pragma unroll
-        for (int k = 0; k < 3; ++k) v[k] = zp[k];
+          for (int k = 0; k < 3; ++k) v[i][k] = sp[k];
+        }
       }
-      uint2* dp = reinterpret_cast<uint2*>(wout + (long long)i * cs);
+    }
 #pragma unroll
-      for (int k = 0; k < 3; ++k) dp[k] = v[k];
+    for (int i = 0; i < DEC_MAXW0; ++i) {
+      if (i < W0) {
+        uint2* dp = reinterpret_cast<uint2*>(wout + (long long)i * cs);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) dp[k] = v[i][k];
+      }
     }
   }
 }
@@ -777,7 +786,7 @@ __global__ void __launch_bounds__(FAST_THREADS, 4)
 decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   pdl_entry();
   constexpr int HIST = K - 1;
-  constexpr int U = 8;  // window columns in flight
+  constexpr int U = 6;  // window columns in flight
   const int r = blockIdx.x;
   const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
   if (h >= P.H) return;
@@ -846,14 +855,24 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
   float* dbase[VQ];
 #pragma unroll
   for (int p = 0; p < VQ; ++p) dbase[p] = st + (dok[p] ? dst[p] : 0) * A.inner_state.block_stride + h;
+  // the taps of a chunk are loaded with its window columns, a chunk ahead
+  // (read-only loads: nothing orders them after the snapshot stores)
+  uint2 wc[U];
+#pragma unroll
+  for (int t = 0; t < U; ++t)
+    wc[t] = t < HIST ? __ldg(reinterpret_cast<const uint2*>(w + (long long)t * wk)) : make_uint2(0u, 0u);
 #pragma unroll 1
   for (int k0 = 0; k0 < HIST; k0 += U) {
     float4 nx[U];
+    uint2 wn[U];
 #pragma unroll
-    for (int t = 0; t < U; ++t)
+    for (int t = 0; t < U; ++t) {
       nx[t] = (src_ok && k0 + U + t < HIST)
                   ? *reinterpret_cast<const float4*>(sp + (long long)(k0 + U + t) * cs)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      wn[t] = k0 + U + t < HIST ? __ldg(reinterpret_cast<const uint2*>(w + (long long)(k0 + U + t) * wk))
+                                : make_uint2(0u, 0u);
+    }
 #pragma unroll
     for (int t = 0; t < U; ++t) {
       const int k = k0 + t;
@@ -862,7 +881,11 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
         for (int j = VQ - 1; j > 0; --j)
 #pragma unroll
           for (int c = 0; c < 4; ++c) wr[j][c] = wr[j - 1][c];
-        load_bf16x4(w + (long long)k * wk, wr[0]);
+        {
+          const float2 a = __bfloat1622float2(as_bf162(wc[t].x));
+          const float2 b = __bfloat1622float2(as_bf162(wc[t].y));
+          wr[0][0] = a.x; wr[0][1] = a.y; wr[0][2] = b.x; wr[0][3] = b.y;
+        }
         const float sx[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
 #pragma unroll
         for (int p = 0; p < VQ; ++p) {
@@ -876,7 +899,10 @@ decode_fir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
       }
     }
 #pragma unroll
-    for (int t = 0; t < U; ++t) sv[t] = nx[t];
+    for (int t = 0; t < U; ++t) {
+      sv[t] = nx[t];
+      wc[t] = wn[t];
+    }
   }
   // ---- short filter of the 4 channels' triples, window shift (after the
   // stream, so that its values are not held in registers across it)
@@ -954,66 +980,92 @@ static bool fir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& 
 
 // LI verify (q <= VQ positions per request, speculative windows, S2 rows of
 // D = 16 .. 20 floats: the 16 modes, then padding columns, the last of channel
-// 0 holding the block's position stamp).  A block covers 64 channels of LV_R
-// requests, whose rows form one contiguous, 16-byte-aligned run of 64 D floats
-// per state block:
-//   1. every request's source run is put in flight into shared memory (16-byte
-//      cp.async) before anything else;
-//   2. one thread per (request, 4 channels) runs the short filter
+// 0 holding the block's position stamp).  Every warp works on its own, with no
+// block barrier: 32 channels (one per lane) of LW_R requests, whose rows form
+// one contiguous, 16-byte-aligned run of 32 D floats per state block.
+//   1. lanes 0 .. LW_R-1 resolve one request each (every routing load at once);
+//   2. the requests' source runs are put in flight into the warp's shared
+//      memory (16-byte cp.async);
+//   3. lane (request i, quad c) runs the short filter of channels 4c .. 4c+3
 //      (verify_gate4), x2 and u to shared memory;
-//   3. four threads per channel, four modes each (the quad layout of
-//      decode_iir_q1_kernel), advance the state position by position: each
-//      snapshot is written over the modes of the run in shared memory and every
-//      warp stores its 8 channels' rows (8 D floats) with 16-byte stores.  The
-//      padding columns so travel from the source block, except channel 0's
-//      (the stamp), which are never written;
-//   4. the (request, 4 channels) threads apply D and the x2 gate, 8-byte stores.
+//   4. each lane advances its channel's 16 modes position by position in
+//      packed f32x2 arithmetic (two modes per instruction, the same roundings):
+//      each snapshot is written over the channel's modes in the run and the
+//      warp stores the run with 16-byte stores, so the padding columns travel
+//      from the source block, except channel 0's (the stamp), which are never
+//      written; the readout (modal_readout16_x2), D and the x2 gate follow.
 // Same arithmetic, order and rounding as decode_kernel.
-constexpr int LV_R = 4;
-constexpr int LV_CH = 64;
-constexpr int LV_THREADS = 256;
-static_assert(LV_R * LV_CH / 4 <= LV_THREADS, "one gate item per thread");
+constexpr int LW_R = 4;        // requests per warp: 8 gate items each fill the warp
+constexpr int LW_WARPS = 4;    // warps (32-channel groups) per block
 
-__global__ void __launch_bounds__(LV_THREADS, 2)
+struct LwMeta {
+  float u[LW_R][VQ][32], x2[LW_R][VQ][32];
+  long long src[LW_R], cin[LW_R], cout[LW_R], dst[LW_R][VQ];
+  int t0[LW_R], n[LW_R], off[LW_R], flags[LW_R];
+};
+static_assert(sizeof(LwMeta) % 16 == 0, "runs follow the metadata 16-byte aligned");
+// dynamic shared memory per warp: the metadata, then LW_R runs of 32 D floats
+__host__ __device__ constexpr int lw_warp_bytes(int D) { return (int)sizeof(LwMeta) + LW_R * 32 * D * 4; }
+
+__global__ void __launch_bounds__(LW_WARPS * 32)
 decode_iir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) {
-  __shared__ __align__(16) float run_sm[LV_R][LV_CH * IIR_STAGE_MAXD];
-  __shared__ float u_s[LV_R][VQ][LV_CH], x2_s[LV_R][VQ][LV_CH], y_s[LV_R][VQ][LV_CH];
-  __shared__ long long rt_cin[LV_R], rt_cout[LV_R], rt_src[LV_R], rt_dst[LV_R][VQ];
-  __shared__ int rt_t0[LV_R], rt_n[LV_R], rt_off[LV_R], rt_flags[LV_R];
-  constexpr int F_ZERO = 1, F_SRC = 2, F_CONV = 4;  // rt_flags bits; dst p ok: bit 8 + p
+  extern __shared__ __align__(16) uint8_t lw_sm[];
+  constexpr int F_ZERO = 1, F_SRC = 2, F_CONV = 4;  // flags; snapshot p written: bit 8 + p
   pdl_entry();
-  const int hb = blockIdx.x * LV_CH, r0 = blockIdx.y * LV_R;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int D = (int)A.inner_state.dim_stride;
+  LwMeta& M = *reinterpret_cast<LwMeta*>(lw_sm + warp * lw_warp_bytes(D));
+  float* runs = reinterpret_cast<float*>(lw_sm + warp * lw_warp_bytes(D) + sizeof(LwMeta));
+  const int h0 = (blockIdx.x * LW_WARPS + warp) * 32;  // the warp's first channel
+  if (h0 >= P.H) return;  // whole warps only: no block-wide barrier follows
+  const int r0 = blockIdx.y * LW_R;
   const long long bs = A.inner_state.block_stride;
   float* st = static_cast<float*>(A.inner_state.data);
-  if (threadIdx.x < LV_R) {
-    const int i = threadIdx.x, r = r0 + i;
+
+  // 1. routing
+  if (lane < LW_R) {
+    const int i = lane, r = r0 + i;
     int t0 = 0, n = 0, off = 0, fl = 0;
     long long cin = -1, cout = -1, src = -1;
+    long long ins[VQ], outs[VQ];
+#pragma unroll
+    for (int p = 0; p < VQ; ++p) ins[p] = outs[p] = -1;
     if (r < A.num_reqs) {
+      // the slot tables' q <= VQ columns are read whole, the accepted one
+      // picked afterwards
+      t0 = r;
+      int t1 = r + 1;
       if (A.token_start) {
         t0 = __ldg(A.token_start + r);
-        n = __ldg(A.token_start + r + 1) - t0;
-      } else {
-        t0 = r;
-        n = 1;
+        t1 = __ldg(A.token_start + r + 1);
       }
+      int acc = A.accepted ? __ldg(A.accepted + r) : 1;
+      cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+      cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
+#pragma unroll
+      for (int p = 0; p < VQ; ++p) {
+        if (p < A.q) {
+          ins[p] = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)p * A.in_stride1);
+          outs[p] = __ldg(A.out_slots + (long long)r * A.out_stride0 + (long long)p * A.out_stride1);
+        }
+      }
+      n = t1 - t0;
       if (n > A.q || n > VQ) {
         flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
         n = min(A.q, VQ);
       }
       n = max(n, 0);
-    }
-    if (n > 0) {
-      int acc = A.accepted ? max(1, __ldg(A.accepted + r)) : 1;
+      acc = max(1, acc);
       if (acc > A.q) {  // past the slot table's columns
-        flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
+        if (n > 0) flag_error(A.error_flags, HYENA_FLAG_SEGMENT);
         acc = A.q;
       }
       off = acc - 1;
-      cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
-      cout = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
-      src = __ldg(A.in_slots + (long long)r * A.in_stride0 + (long long)off * A.in_stride1);
+#pragma unroll
+      for (int p = 0; p < VQ; ++p)
+        if (p == off) src = ins[p];
+    }
+    if (n > 0) {
       const bool cin_ok = block_ok(cin, A.conv_state);
       if ((A.zero_null_rows && cin == A.null_block) || !cin_ok) fl |= F_ZERO;
       if (block_ok(src, A.inner_state)) fl |= F_SRC;
@@ -1021,92 +1073,113 @@ decode_iir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
         fl |= F_CONV;
       if (!cin_ok || (!(fl & F_ZERO) && !(fl & F_SRC)))
         flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-#pragma unroll
-      for (int p = 0; p < VQ; ++p) {
-        long long d = -1;
-        if (p < n) {
-          d = __ldg(A.out_slots + (long long)r * A.out_stride0 + (long long)p * A.out_stride1);
-          if (!(fl & F_ZERO) && block_ok(d, A.inner_state) &&
-              !(A.skip_null_writes && d == A.null_block))
-            fl |= 256 << p;
-        }
-        rt_dst[i][p] = d;
-      }
     }
-    rt_t0[i] = t0;
-    rt_n[i] = n;
-    rt_off[i] = off;
-    rt_flags[i] = fl;
-    rt_cin[i] = cin;
-    rt_cout[i] = cout;
-    rt_src[i] = src;
+#pragma unroll
+    for (int p = 0; p < VQ; ++p) {
+      const long long d = p < n ? outs[p] : -1;
+      if (p < n && !(fl & F_ZERO) && block_ok(d, A.inner_state) &&
+          !(A.skip_null_writes && d == A.null_block))
+        fl |= 256 << p;
+      M.dst[i][p] = d;
+    }
+    M.t0[i] = t0;
+    M.n[i] = n;
+    M.off[i] = off;
+    M.flags[i] = fl;
+    M.cin[i] = cin;
+    M.cout[i] = cout;
+    M.src[i] = src;
   }
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int t = lane & 3;                 // modes 4t .. 4t+3
-  const int cl = warp * 8 + (lane >> 2);  // channel within the block
-  const float4 lp4 = __ldg(reinterpret_cast<const float4*>(P.log_poles + (long long)(hb + cl) * P.lp_stride_h) + t);
-  const float4 rs4 = __ldg(reinterpret_cast<const float4*>(P.residues + (long long)(hb + cl) * P.res_stride_h) + t);
-  __syncthreads();
+  __syncwarp();
 
-  // 1. source runs: 16 D chunks of 16 bytes per request
-  const int chunks = 16 * D;
-  for (int j = threadIdx.x; j < LV_R * chunks; j += LV_THREADS) {
-    const int i = j / chunks, c = j - i * chunks;
-    if (rt_n[i] == 0 || (rt_flags[i] & F_ZERO)) continue;
-    float* d = &run_sm[i][4 * c];
-    if (rt_flags[i] & F_SRC)
-      cp_async16(d, st + rt_src[i] * bs + (long long)hb * D + 4 * c);
-    else
-      *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
+  // 2. source runs: 8 D chunks of 16 bytes per request
+  const int chunks = 8 * D;
+#pragma unroll 1
+  for (int i = 0; i < LW_R; ++i) {
+    const int fl = M.flags[i];
+    if (M.n[i] == 0 || (fl & F_ZERO)) continue;  // uniform
+    float* run = runs + i * 32 * D;
+    const float* sp = st + M.src[i] * bs + (long long)h0 * D;
+    for (int c = lane; c < chunks; c += 32) {
+      if (fl & F_SRC)
+        cp_async16(run + 4 * c, sp + 4 * c);
+      else
+        *reinterpret_cast<float4*>(run + 4 * c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   cp_async_commit();
 
-  // 2. short filter + gate, item = (request i, channels 4 c4 .. 4 c4 + 3)
-  const int gi = threadIdx.x / (LV_CH / 4), gc = threadIdx.x % (LV_CH / 4);
-  const bool gate_item = threadIdx.x < LV_R * LV_CH / 4;
-  if (gate_item && rt_n[gi] > 0 && !(rt_flags[gi] & F_ZERO)) {
-    float x2v[VQ][4], uv[VQ][4];
-    verify_gate4<VQ>(P, A, hb + 4 * gc, rt_t0[gi], rt_n[gi], rt_off[gi], rt_cin[gi], rt_cout[gi],
-                     (rt_flags[gi] & F_CONV) != 0, x2v, uv);
+  // 3. short filter + gate: lane = (request i, channels 4 c .. 4 c + 3)
+  {
+    const int i = lane >> 3, c = lane & 7;
+    if (M.n[i] > 0 && !(M.flags[i] & F_ZERO)) {
+      float x2v[VQ][4], uv[VQ][4];
+      verify_gate4<VQ>(P, A, h0 + 4 * c, M.t0[i], M.n[i], M.off[i], M.cin[i], M.cout[i],
+                       (M.flags[i] & F_CONV) != 0, x2v, uv);
 #pragma unroll
-    for (int p = 0; p < VQ; ++p)
+      for (int p = 0; p < VQ; ++p)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        x2_s[gi][p][4 * gc + c] = x2v[p][c];
-        u_s[gi][p][4 * gc + c] = uv[p][c];
-      }
+        for (int k = 0; k < 4; ++k) {
+          M.x2[i][p][4 * c + k] = x2v[p][k];
+          M.u[i][p][4 * c + k] = uv[p][k];
+        }
+    }
   }
-  cp_async_wait<0>();
-  __syncthreads();
-
-  // 3. modal recurrence, snapshots, readout
-  const float pole[4] = {expf(lp4.x), expf(lp4.y), expf(lp4.z), expf(lp4.w)};
-  const float res[4] = {rs4.x, rs4.y, rs4.z, rs4.w};
-  const bool stamp_rows = D > 16 && hb == 0 && warp == 0;  // chunk 4 holds channel 0's columns 16..
-#pragma unroll 1
-  for (int i = 0; i < LV_R; ++i) {
-    const int n = rt_n[i], fl = rt_flags[i];
-    if (n == 0 || (fl & F_ZERO)) continue;  // uniform
-    float* runp = run_sm[i];
-    float s4[4];
+  const int h = h0 + lane;
+  float2 pl2[8], rs2[8];
+  {
+    const float4* lp4 = reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h);
+    const float4* rs4 = reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) s4[m] = runp[cl * D + 4 * t + m];
+    for (int k = 0; k < 4; ++k) {
+      const float4 a = __ldg(lp4 + k), b = __ldg(rs4 + k);
+      pl2[2 * k] = make_float2(expf(a.x), expf(a.y));
+      pl2[2 * k + 1] = make_float2(expf(a.z), expf(a.w));
+      rs2[2 * k] = make_float2(b.x, b.y);
+      rs2[2 * k + 1] = make_float2(b.z, b.w);
+    }
+  }
+  const bf16* Dg = static_cast<const bf16*>(P.D);
+  const float dval = Dg ? ldbf(Dg + h) : 0.0f;
+  cp_async_wait<0>();
+  __syncwarp();
+
+  // 4. modal recurrence, snapshots, readout, output gate
+  const bool stamp_run = D > 16 && h0 == 0;  // chunk 4 holds channel 0's columns 16 ..
+  bf16* outp = static_cast<bf16*>(A.out) + h;
+#pragma unroll 1
+  for (int i = 0; i < LW_R; ++i) {
+    const int n = M.n[i], fl = M.flags[i];
+    if (n == 0) continue;  // uniform
+    const int t0 = M.t0[i];
+    if (fl & F_ZERO) {
+      for (int p = 0; p < n; ++p) outp[(long long)(t0 + p) * A.ldo] = __float2bfloat16_rn(0.0f);
+      continue;
+    }
+    float* run = runs + i * 32 * D;
+    float* mine = run + lane * D;  // odd D: the lanes' rows hit distinct banks
+    float2 s2[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s2[k] = make_float2(mine[2 * k], mine[2 * k + 1]);
 #pragma unroll
     for (int p = 0; p < VQ; ++p) {
       if (p >= n) break;  // uniform
-      const float u = u_s[i][p][cl];
+      const float u = M.u[i][p][lane];
+      const float2 u2 = make_float2(u, u);
 #pragma unroll
-      for (int m = 0; m < 4; ++m) s4[m] = add_rn(mul_rn(s4[m], pole[m]), u);
+      for (int k = 0; k < 8; ++k) s2[k] = fadd2(fmul2(s2[k], pl2[k]), u2);
       if (fl & (256 << p)) {  // uniform
         __syncwarp();  // the previous snapshot's stores have read the run
 #pragma unroll
-        for (int m = 0; m < 4; ++m) runp[cl * D + 4 * t + m] = s4[m];
+        for (int k = 0; k < 8; ++k) {
+          mine[2 * k] = s2[k].x;
+          mine[2 * k + 1] = s2[k].y;
+        }
         __syncwarp();
-        const float* sp = runp + 8 * warp * D;
-        float* dp = st + rt_dst[i][p] * bs + (long long)(hb + 8 * warp) * D;
-        for (int j = lane; j < 2 * D; j += 32) {
-          const float4 v = *reinterpret_cast<const float4*>(sp + 4 * j);
-          if (stamp_rows && j == 4) {
+        float* dp = st + M.dst[i][p] * bs + (long long)h0 * D;
+        for (int j = lane; j < chunks; j += 32) {
+          const float4 v = *reinterpret_cast<const float4*>(run + 4 * j);
+          if (stamp_run && j == 4) {
             const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -1116,33 +1189,9 @@ decode_iir_verify_kernel(const hyena_layer_params P, const hyena_decode_args A) 
           }
         }
       }
-      const float yr = quad_readout(s4, res);
-      if (t == 0) y_s[i][p][cl] = yr;
-    }
-  }
-  __syncthreads();
-
-  // 4. output gate
-  if (gate_item && rt_n[gi] > 0) {
-    const int n = rt_n[gi], t0 = rt_t0[gi];
-    bf16* out = static_cast<bf16*>(A.out) + hb + 4 * gc;
-    if (rt_flags[gi] & F_ZERO) {
-      const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int p = 0; p < n; ++p) store_bf16x4(out + (long long)(t0 + p) * A.ldo, zero);
-    } else {
-      const bf16* Dg = static_cast<const bf16*>(P.D);
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      if (Dg) load_bf16x4(Dg + hb + 4 * gc, d);
-      for (int p = 0; p < n; ++p) {
-        float g[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float yy = bf16r(y_s[gi][p][4 * gc + c]);
-          if (Dg) yy = bf16r(yy + bf16r(d[c] * u_s[gi][p][4 * gc + c]));
-          g[c] = bf16r(x2_s[gi][p][4 * gc + c] * yy);
-        }
-        store_bf16x4(out + (long long)(t0 + p) * A.ldo, g);
-      }
+      float y = bf16r(modal_readout16_x2(s2, rs2));
+      if (Dg) y = bf16r(y + bf16r(dval * u));
+      outp[(long long)(t0 + p) * A.ldo] = __float2bfloat16_rn(bf16r(M.x2[i][p][lane] * y));
     }
   }
 }
@@ -1155,7 +1204,7 @@ static bool iir_verify_ok(const hyena_layer_params& P, const hyena_decode_args& 
   return s.col_stride == 1 && s.dim_stride >= 16 && s.dim_stride <= IIR_STAGE_MAXD &&
          aligned_elems(s.data, s.block_stride, 4, 16) && P.lp_stride_s == 1 &&
          P.res_stride_s == 1 && aligned_elems(P.log_poles, P.lp_stride_h, 4, 16) &&
-         aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % LV_CH == 0;
+         aligned_elems(P.residues, P.res_stride_h, 4, 16) && P.H % 32 == 0;
 }
 
 int decode_launch(const hyena_layer_params& P, const hyena_decode_args& args, cudaStream_t st) {
@@ -1189,8 +1238,12 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& args, cu
     return check_launch("decode_fir_verify_kernel");
   }
   if (iir_verify_ok(P, A)) {
-    dim3 g(P.H / LV_CH, (A.num_reqs + LV_R - 1) / LV_R);
-    launch_kernel(decode_iir_verify_kernel, dim3(g), dim3(LV_THREADS), 0, st, 0u, P, A);
+    const int bytes = LW_WARPS * lw_warp_bytes((int)A.inner_state.dim_stride);
+    if (!smem_attr<decode_iir_verify_kernel>(LW_WARPS * lw_warp_bytes(IIR_STAGE_MAXD)))
+      return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(decode_iir_verify_kernel)");
+    dim3 g((P.H / 32 + LW_WARPS - 1) / LW_WARPS, (A.num_reqs + LW_R - 1) / LW_R);
+    launch_kernel(decode_iir_verify_kernel, dim3(g), dim3(LW_WARPS * 32), (size_t)bytes, st, 0u,
+                  P, A);
     return check_launch("decode_iir_verify_kernel");
   }
   dim3 grid(A.num_reqs, (P.H + DEC_THREADS - 1) / DEC_THREADS);
