@@ -691,22 +691,27 @@ __device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const 
   uint2 swr[9];  // 36 taps: column j's three at 3j
 #pragma unroll
   for (int i = 0; i < 9; ++i) swr[i] = __ldg(swv + i);
-  // tap e of the 36 (e known at compile time after unrolling: stays in registers)
-  auto tap = [&](int e) {
-    const uint32_t w = (e & 2) ? swr[e >> 2].y : swr[e >> 2].x;
-    return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
-  };
-  float c0[12], c1[12];
+  // The 12 columns run as 6 bf16x2 column pairs (2j, 2j+1) through short_tap2,
+  // which rounds each product to bf16 and sums in fp32 exactly as short_tap.
+  // wp[j][k]: tap k of the pair, from taps e = 3 col + k (word e / 2, half e % 2).
+  auto tap_word = [&](int i) -> uint32_t { return (i & 1) ? swr[i >> 1].y : swr[i >> 1].x; };
+  bf162 wp[6][3];
 #pragma unroll
-  for (int i = 0; i < 12; i += 4) {
-    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-    if (off < W0) load_bf16x4(win + (long long)off * cs + i, a);
-    if (off + 1 < W0) load_bf16x4(win + (long long)(off + 1) * cs + i, b);
+  for (int j = 0; j < 6; ++j)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      c0[i + k] = a[k];
-      c1[i + k] = b[k];
+    for (int k = 0; k < 3; ++k) {
+      const int e1 = 6 * j + k, e2 = 6 * j + 3 + k;
+      const uint32_t sel = ((e1 & 1) ? 0x0032u : 0x0010u) | ((e2 & 1) ? 0x7600u : 0x5400u);
+      wp[j][k] = as_bf162(__byte_perm(tap_word(e1 >> 1), tap_word(e2 >> 1), sel));
     }
+  uint32_t c0[6], c1[6];  // window columns off, off + 1 as column-pair words
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    uint2 a = make_uint2(0u, 0u), b = make_uint2(0u, 0u);
+    if (off < W0) a = *reinterpret_cast<const uint2*>(win + (long long)off * cs + 4 * i);
+    if (off + 1 < W0) b = *reinterpret_cast<const uint2*>(win + (long long)(off + 1) * cs + 4 * i);
+    c0[2 * i] = a.x; c0[2 * i + 1] = a.y;
+    c1[2 * i] = b.x; c1[2 * i + 1] = b.y;
   }
   const bf16* z = static_cast<const bf16*>(A.z);
 #pragma unroll
@@ -715,25 +720,33 @@ __device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const 
     for (int c = 0; c < 4; ++c) x2v[p][c] = uv[p][c] = 0.0f;
     if (p < n) {
       const uint2* zp = reinterpret_cast<const uint2*>(z + (long long)(t0 + p) * A.ldz + 3 * h);
-      float xz[12];
+      uint32_t o[6];
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         const uint2 zw = zp[i];
-        const float2 a = __bfloat1622float2(as_bf162(zw.x));
-        const float2 b = __bfloat1622float2(as_bf162(zw.y));
-        xz[4 * i] = a.x; xz[4 * i + 1] = a.y; xz[4 * i + 2] = b.x; xz[4 * i + 3] = b.y;
-      }
-      float o[12];
+        const uint32_t xw[2] = {zw.x, zw.y};
 #pragma unroll
-      for (int j = 0; j < 12; ++j) {
-        o[j] = short_tap(c0[j], c1[j], xz[j], tap(3 * j), tap(3 * j + 1), tap(3 * j + 2));
-        c0[j] = c1[j];
-        c1[j] = xz[j];
+        for (int e = 0; e < 2; ++e) {
+          const int j = 2 * i + e;
+          o[j] = as_u32(short_tap2(as_bf162(c0[j]), as_bf162(c1[j]), as_bf162(xw[e]), wp[j][0],
+                                   wp[j][1], wp[j][2]));
+          c0[j] = c1[j];
+          c1[j] = xw[e];
+        }
       }
+      // channel c's (x2, x1, v) are columns 3c .. 3c+2: words (w0, w1, w2) of
+      // channels (0, 1) hold (x2_0, x1_0), (v_0, x2_1), (x1_1, v_1); likewise
+      // (w3, w4, w5) for channels (2, 3).  u = bf16(x1 v) is one bf16x2 product.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        x2v[p][c] = o[3 * c];
-        uv[p][c] = bf16r(o[3 * c + 1] * o[3 * c + 2]);
+      for (int hp = 0; hp < 2; ++hp) {
+        const uint32_t w0 = o[3 * hp], w1 = o[3 * hp + 1], w2 = o[3 * hp + 2];
+        const float2 x2 = __bfloat1622float2(as_bf162(__byte_perm(w0, w1, 0x7610)));
+        const float2 u2 = __bfloat1622float2(__hmul2(as_bf162(__byte_perm(w0, w2, 0x5432)),
+                                                     as_bf162(__byte_perm(w1, w2, 0x7610))));
+        x2v[p][2 * hp] = x2.x;
+        x2v[p][2 * hp + 1] = x2.y;
+        uv[p][2 * hp] = u2.x;
+        uv[p][2 * hp + 1] = u2.y;
       }
     }
   }
