@@ -355,6 +355,54 @@ __device__ __forceinline__ void store_bf16x4(bf16* p, const float (&v)[4]) {
   *reinterpret_cast<uint2*>(p) = r;
 }
 
+// The K=3 short filter of 4 consecutive channels' triples: their 12 z columns
+// as 6 bf16x2 column pairs (2j, 2j+1) through short_tap2, which rounds each
+// product to bf16 and sums oldest first in fp32 exactly as short_tap does.
+struct Taps4 {
+  bf162 w[6][3];  // tap k of column pair j
+};
+// From the 36 contiguous short taps of the 4 channels (tap e = 3 col + k sits
+// in word e / 2, half e % 2).
+__device__ __forceinline__ Taps4 taps4(const uint2 (&swr)[9]) {
+  auto word = [&](int i) -> uint32_t { return (i & 1) ? swr[i >> 1].y : swr[i >> 1].x; };
+  Taps4 T;
+#pragma unroll
+  for (int j = 0; j < 6; ++j)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int e1 = 6 * j + k, e2 = 6 * j + 3 + k;
+      const uint32_t sel = ((e1 & 1) ? 0x0032u : 0x0010u) | ((e2 & 1) ? 0x7600u : 0x5400u);
+      T.w[j][k] = as_bf162(__byte_perm(word(e1 >> 1), word(e2 >> 1), sel));
+    }
+  return T;
+}
+// o = the filter outputs of one row x from the window rows c0 (older) and c1.
+__device__ __forceinline__ void short4(const Taps4& T, const uint32_t (&c0)[6],
+                                       const uint32_t (&c1)[6], const uint32_t (&x)[6],
+                                       uint32_t (&o)[6]) {
+#pragma unroll
+  for (int j = 0; j < 6; ++j)
+    o[j] = as_u32(short_tap2(as_bf162(c0[j]), as_bf162(c1[j]), as_bf162(x[j]), T.w[j][0],
+                             T.w[j][1], T.w[j][2]));
+}
+// Channel c's (x2, x1, v) are columns 3c .. 3c+2: words (w0, w1, w2) of channels
+// (0, 1) hold (x2_0, x1_0), (v_0, x2_1), (x1_1, v_1); likewise (w3, w4, w5) for
+// channels (2, 3).  u = bf16(x1 v) is one bf16x2 product (exact product, one
+// rounding: bf16r(x1 * v)).
+__device__ __forceinline__ void split4(const uint32_t (&o)[6], float (&x2)[4], float (&u)[4]) {
+#pragma unroll
+  for (int hp = 0; hp < 2; ++hp) {
+    const uint32_t w0 = o[3 * hp], w1 = o[3 * hp + 1], w2 = o[3 * hp + 2];
+    const float2 a = __bfloat1622float2(as_bf162(__byte_perm(w0, w1, 0x7610)));
+    const float2 b = __bfloat1622float2(__hmul2(as_bf162(__byte_perm(w0, w2, 0x5432)),
+                                                as_bf162(__byte_perm(w1, w2, 0x7610))));
+    x2[2 * hp] = a.x;
+    x2[2 * hp + 1] = a.y;
+    u[2 * hp] = b.x;
+    u[2 * hp + 1] = b.y;
+  }
+}
+
 // Short filter + gate for `C` consecutive channels starting at h, in two
 // halves so that callers can put its loads in flight together with their own:
 // gate_load reads the triple row of z, window columns 0, 1 of S0 (block cin)
@@ -691,19 +739,7 @@ __device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const 
   uint2 swr[9];  // 36 taps: column j's three at 3j
 #pragma unroll
   for (int i = 0; i < 9; ++i) swr[i] = __ldg(swv + i);
-  // The 12 columns run as 6 bf16x2 column pairs (2j, 2j+1) through short_tap2,
-  // which rounds each product to bf16 and sums in fp32 exactly as short_tap.
-  // wp[j][k]: tap k of the pair, from taps e = 3 col + k (word e / 2, half e % 2).
-  auto tap_word = [&](int i) -> uint32_t { return (i & 1) ? swr[i >> 1].y : swr[i >> 1].x; };
-  bf162 wp[6][3];
-#pragma unroll
-  for (int j = 0; j < 6; ++j)
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      const int e1 = 6 * j + k, e2 = 6 * j + 3 + k;
-      const uint32_t sel = ((e1 & 1) ? 0x0032u : 0x0010u) | ((e2 & 1) ? 0x7600u : 0x5400u);
-      wp[j][k] = as_bf162(__byte_perm(tap_word(e1 >> 1), tap_word(e2 >> 1), sel));
-    }
+  const Taps4 T = taps4(swr);
   uint32_t c0[6], c1[6];  // window columns off, off + 1 as column-pair words
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
@@ -720,34 +756,20 @@ __device__ __forceinline__ void verify_gate4(const hyena_layer_params& P, const 
     for (int c = 0; c < 4; ++c) x2v[p][c] = uv[p][c] = 0.0f;
     if (p < n) {
       const uint2* zp = reinterpret_cast<const uint2*>(z + (long long)(t0 + p) * A.ldz + 3 * h);
-      uint32_t o[6];
+      uint32_t xw[6], o[6];
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         const uint2 zw = zp[i];
-        const uint32_t xw[2] = {zw.x, zw.y};
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = 2 * i + e;
-          o[j] = as_u32(short_tap2(as_bf162(c0[j]), as_bf162(c1[j]), as_bf162(xw[e]), wp[j][0],
-                                   wp[j][1], wp[j][2]));
-          c0[j] = c1[j];
-          c1[j] = xw[e];
-        }
+        xw[2 * i] = zw.x;
+        xw[2 * i + 1] = zw.y;
       }
-      // channel c's (x2, x1, v) are columns 3c .. 3c+2: words (w0, w1, w2) of
-      // channels (0, 1) hold (x2_0, x1_0), (v_0, x2_1), (x1_1, v_1); likewise
-      // (w3, w4, w5) for channels (2, 3).  u = bf16(x1 v) is one bf16x2 product.
+      short4(T, c0, c1, xw, o);
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp) {
-        const uint32_t w0 = o[3 * hp], w1 = o[3 * hp + 1], w2 = o[3 * hp + 2];
-        const float2 x2 = __bfloat1622float2(as_bf162(__byte_perm(w0, w1, 0x7610)));
-        const float2 u2 = __bfloat1622float2(__hmul2(as_bf162(__byte_perm(w0, w2, 0x5432)),
-                                                     as_bf162(__byte_perm(w1, w2, 0x7610))));
-        x2v[p][2 * hp] = x2.x;
-        x2v[p][2 * hp + 1] = x2.y;
-        uv[p][2 * hp] = u2.x;
-        uv[p][2 * hp + 1] = u2.y;
+      for (int j = 0; j < 6; ++j) {
+        c0[j] = c1[j];
+        c1[j] = xw[j];
       }
+      split4(o, x2v[p], uv[p]);
     }
   }
   if (write_conv) {
