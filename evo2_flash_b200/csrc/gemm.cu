@@ -721,6 +721,258 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
   }
 }
 
+// ---------------------------------------------------------------- 2-SM tiles
+// Large M: a cluster of two CTAs (an SM pair) computes 256 x 256 output tiles
+// with tcgen05.mma.cta_group::2.  CTA r of the pair stages rows [128 r, 128 r +
+// 128) of the A slab and rows [128 r, 128 r + 128) of the B slab (weight rows,
+// i.e. output columns) in its own ring; the MMA, issued by the even CTA, reads
+// both CTAs' stages at the same offsets and leaves each CTA's 128 output rows x
+// 256 columns in that CTA's tensor memory.  Per CTA and 128-byte K slab that is
+// 32 KB of operands for a 128 x 256 product (48 KB with a 1-SM tile of the same
+// size), so L2 serves a third less and six stages fit instead of four.
+//   warp 0 (both CTAs)  TMA of the CTA's halves; every copy completes on the
+//                       even CTA's "full" barrier, which expects both halves
+//   warp 1 (even CTA)   MMA issue; a stage is released by a commit multicast to
+//                       both CTAs' "empty" barriers, an accumulator by one to
+//                       both CTAs' "acc_full"
+//   warps 2-5           epilogue of the CTA's 128 rows; the accumulator goes back
+//                       by arrivals (4 per CTA) on the even CTA's "acc_empty"
+// Tensor memory is allocated pair-wise (cta_group::2, 2 x 256 columns).
+constexpr int BN2 = 256;
+struct Cfg2 {
+  static constexpr int A_BYTES = BM * BKB;
+  static constexpr int B_BYTES = (BN2 / 2) * BKB;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr uint32_t TMEM_COLS = 2 * BN2;
+};
+struct __align__(1024) Smem2 {
+  uint8_t a[Cfg2::STAGES][Cfg2::A_BYTES];
+  uint8_t b[Cfg2::STAGES][Cfg2::B_BYTES];
+  uint64_t full[Cfg2::STAGES];
+  uint64_t empty[Cfg2::STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+// TMA tile load by either CTA of a pair, completing on the mbarrier at cluster
+// address `bar` (the even CTA's).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar, void* dst,
+                                                 int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+template <bool FP8>
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  if constexpr (FP8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  }
+}
+// Arrive (once) on the mbarrier at the same offset in both CTAs of the pair
+// when every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(su32(bar)),
+      "h"(both)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+template <bool FP8>
+__host__ __device__ constexpr uint32_t idesc_pair() {
+  return (1u << 4) | ((FP8 ? 0u : 1u) << 7) | ((FP8 ? 0u : 1u) << 10) |
+         (uint32_t(BN2 >> 3) << 17) | (uint32_t((2 * BM) >> 4) << 24);
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
+                 const float* __restrict__ sa, const float* __restrict__ sb,
+                 const bf16* __restrict__ bias) {
+  pdl_trigger();
+  constexpr int STAGES = Cfg2::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  Smem2& S = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int ELEM = FP8 ? 1 : 2;
+  constexpr int KE = BKB / ELEM;
+  const int kblocks = K / KE;
+  const uint32_t rank = cluster_rank();  // 0: the MMA-issuing CTA
+  const int pair = (int)blockIdx.x / 2, npairs = (int)gridDim.x / 2;
+  const int n_tiles = (N + BN2 - 1) / BN2;
+  const int total = n_tiles * ((M + 2 * BM - 1) / (2 * BM));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.acc_full[b], 1);
+      mbar_init(&S.acc_empty[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&S.tmem_base)),
+                 "r"(Cfg2::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  // both CTAs' barriers exist before any copy or arrival can target them
+  cluster_arrive();
+  cluster_wait();
+  fence_after();
+  const uint32_t tmem = S.tmem_base;
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const bool many_m = (M + BM - 1) / BM > 8;
+      const uint64_t pol_a = many_m ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = many_m ? policy_evict_last() : policy_evict_first();
+      const uint32_t full0 = map_to_rank(su32(&S.full[0]), 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total && ok; tile += npairs) {
+        const int m0 = (tile / n_tiles) * 2 * BM + (int)rank * BM;
+        const int n0 = (tile % n_tiles) * BN2 + (int)rank * (BN2 / 2);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&S.empty[s], ((it / STAGES) & 1) ^ 1)) { ok = false; break; }
+          if (rank == 0) mbar_expect_tx(&S.full[s], 2 * Cfg2::STAGE_BYTES);
+          const uint32_t bar = full0 + uint32_t(s * sizeof(uint64_t));
+          tma_load_2d_pair(&tmA, bar, S.a[s], kb * KE, m0, pol_a);
+          tma_load_2d_pair(&tmB, bar, S.b[s], kb * KE, n0, pol_b);
+        }
+      }
+      // Drain: every issued copy has landed before the CTA can exit.  The
+      // even CTA sees its "full" phases complete; the odd CTA sees the MMA
+      // release the stages its copies filled.
+      for (uint32_t i = it > (uint32_t)STAGES ? it - STAGES : 0; i < it; ++i) {
+        if (rank == 0)
+          mbar_wait(&S.full[i % STAGES], (i / STAGES) & 1);
+        else
+          mbar_wait(&S.empty[i % STAGES], (i / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t ID = idesc_pair<FP8>();
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      for (int tile = pair; tile < total && ok; tile += npairs, ++ti) {
+        const int b = ti & 1;
+        if (!mbar_wait(&S.acc_empty[b], ((ti >> 1) & 1) ^ 1)) ok = false;
+        fence_after();
+        const uint32_t d = tmem + uint32_t(b * BN2);
+        for (int kb = 0; kb < kblocks && ok; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(&S.full[s], (it / STAGES) & 1)) { ok = false; break; }
+          fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BKB / 32; ++kk) {
+            const uint64_t ad = sw128_desc(S.a[s] + kk * 32);
+            const uint64_t bd = sw128_desc(S.b[s] + kk * 32);
+            mma_pair<FP8>(d, ad, bd, ID, (kb != 0 || kk != 0) ? 1u : 0u);
+          }
+          mma_commit_pair(&S.empty[s]);
+        }
+        mma_commit_pair(&S.acc_full[b]);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    float scale_a = 1.0f, scale_b = 1.0f;
+    if constexpr (FP8) {
+      scale_a = __ldg(sa);
+      scale_b = __ldg(sb);
+    }
+    const uint32_t acc_empty0 = map_to_rank(su32(&S.acc_empty[0]), 0);
+    uint32_t ti = 0;
+    for (int tile = pair; tile < total; tile += npairs, ++ti) {
+      const int m0 = (tile / n_tiles) * 2 * BM + (int)rank * BM, n0 = (tile % n_tiles) * BN2;
+      const int b = ti & 1;
+      const bool ok = mbar_wait(&S.acc_full[b], (ti >> 1) & 1);
+      if (!ok) break;  // the MMA warp gave up: stop rather than time out per tile
+      fence_after();
+      const int row = m0 + 32 * q + lane;
+#pragma unroll 1
+      for (int cb = 0; cb < BN2 / 32; ++cb) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (uint32_t(32 * q) << 16) + uint32_t(b * BN2 + cb * 32), r);
+        if (cb == BN2 / 32 - 1) {  // accumulator fully read: hand it back to the MMA warp
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc_empty0 + uint32_t(b * sizeof(uint64_t)));
+        }
+        const int col0 = n0 + cb * 32;
+        if (row >= M || col0 >= N) continue;
+        bf16* dst = out + (long long)row * ldo + col0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          if (col0 + 8 * v >= N) break;
+          uint4 pk;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float x0 = __uint_as_float(r[8 * v + 2 * e]);
+            float x1 = __uint_as_float(r[8 * v + 2 * e + 1]);
+            if constexpr (FP8) {
+              x0 = (x0 * scale_a) * scale_b;  // (acc * sx) * sw, fp8_emul.py:87
+              x1 = (x1 * scale_a) * scale_b;
+            } else {
+              if (bias != nullptr) {
+                x0 += __bfloat162float(bias[col0 + 8 * v + 2 * e]);
+                x1 += __bfloat162float(bias[col0 + 8 * v + 2 * e + 1]);
+              }
+            }
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+            pw[e] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          st_stream16(dst + 8 * v, pk);
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  // the pair's MMAs, copies and remote arrivals are over before either CTA
+  // releases tensor memory or exits
+  cluster_arrive();
+  cluster_wait();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(Cfg2::TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -831,9 +1083,76 @@ static int launch_cluster(const CUtensorMap& ta, const void* B, int64_t ldb, voi
   return check_launch(FP8 ? "gemm_cluster_kernel<e4m3>" : "gemm_cluster_kernel<bf16>");
 }
 
+template <bool FP8>
+static int launch_pair(const CUtensorMap& ta, const void* B, int64_t ldb, void* out, int64_t ldo,
+                       int M, int N, int K, const float* sa, const float* sb, const void* bias,
+                       cudaStream_t st) {
+  CUtensorMap tb;
+  int rc = make_map(&tb, B, FP8, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BN2 / 2);
+  if (rc) return rc;
+  const size_t smem = sizeof(Smem2) + 1024;
+  if (!smem_attr<gemm_pair_kernel<FP8>>((int)smem))
+    return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(gemm_pair) failed");
+  const long long tiles = (long long)((N + BN2 - 1) / BN2) * ((M + 2 * BM - 1) / (2 * BM));
+  // the pairs that can be resident at once (SM pairs are formed inside a GPC,
+  // so this can be below half the SMs): a pair launched beyond them would
+  // start its statically assigned tiles only after another pair finished
+  static int resident_pairs[2] = {-1, -1};
+  int& rp = resident_pairs[FP8 ? 1 : 0];
+  if (rp < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<FP8>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    rp = n;
+  }
+  long long cap = rp;
+  const int lim = g_max_ctas.load(std::memory_order_relaxed);
+  if (lim > 0 && lim / 2 < cap) cap = lim / 2 > 0 ? lim / 2 : 1;
+  dim3 grid((unsigned)(2 * (tiles < cap ? tiles : cap)));
+  // Launched without programmatic stream serialisation: its CTAs start only
+  // once the previous kernel in the stream has completed.  (Its own dependents
+  // may still launch early.)  Launched as a programmatic dependent, so that its
+  // pairs became resident beside the previous kernel's still-running CTAs, the
+  // prefill step stalled for good within a few steps, with no bounded wait of
+  // this kernel expiring; launched this way it ran clean.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, ta, tb, static_cast<bf16*>(out), ldo, M, N, K,
+                     sa, sb, static_cast<const bf16*>(bias));
+  return check_launch(FP8 ? "gemm_pair_kernel<e4m3>" : "gemm_pair_kernel<bf16>");
+}
+
 struct Plan {
   int bn, splits;  // splits > 0: cluster kernel with that many K slices per tile
+  bool pair = false;  // 256 x 256 tiles on SM pairs (gemm_pair_kernel)
 };
+
+// Rows from which the SM-pair kernel takes over: enough 256-row tiles that
+// every pair has several and the last wave is short.
+constexpr int PAIR_MIN_M = 4096;
 
 template <bool FP8>
 static int resident(int bn, int splits) {
@@ -857,6 +1176,7 @@ template <bool FP8>
 static Plan plan(int M, int N, int K) {
   const long long mt = (M + BM - 1) / BM;
   const int sms = num_sms();
+  if (M >= PAIR_MIN_M && N >= BN2) return {BN2, 0, true};
   {
     int pick = 0;
     long long pick_cost = 0, cost256 = -1;
@@ -910,6 +1230,7 @@ static int launch(const void* A, int64_t lda, const void* B, int64_t ldb, void* 
   int rc = make_map(&ta, A, FP8, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM);
   if (rc) return rc;
   const Plan pl = plan<FP8>(M, N, K);
+  if (pl.pair) return launch_pair<FP8>(ta, B, ldb, out, ldo, M, N, K, sa, sb, bias, st);
   if (pl.splits > 0) {
     switch (pl.bn) {
       case 256:

@@ -458,9 +458,11 @@ def test_rms_norm_rejects_bad_arguments():
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 384, 512), (1000, 768, 256),
                                    (4096, 12288, 4096), (128, 12288, 4096), (1024, 4096, 4096),
-                                   (7, 4096, 256), (512, 12288, 4096), (500, 12288, 1024)])
+                                   (7, 4096, 256), (512, 12288, 4096), (500, 12288, 1024),
+                                   (4224, 776, 256), (8192, 12288, 512)])
 def test_gemm_e4m3(M, N, K):
-    """(512 | 500, 12288): 192-wide persistent tiles (the q = 4 verify in_proj)."""
+    """(512 | 500, 12288): 192-wide persistent tiles (the q = 4 verify in_proj);
+    M >= 4096: 256 x 256 tiles on SM pairs, with row and column tails (4224 x 776)."""
     from evo2_flash_b200 import ops
 
     g = torch.Generator().manual_seed(M + N)
@@ -477,7 +479,7 @@ def test_gemm_e4m3(M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 512), (1000, 776, 192),
                                    (4096, 4096, 4096), (128, 4096, 4096), (256, 4096, 4096),
-                                   (5, 4104, 128)])
+                                   (5, 4104, 128), (4200, 4104, 128)])
 def test_gemm_bf16_bias(M, N, K):
     from evo2_flash_b200 import ops
 
