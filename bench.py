@@ -53,10 +53,10 @@ PREFILL_B, PREFILL_L = 8, 8192
 DECODE_B = 128
 METRIC = "Hyena-mixer prefill+decode tok/s/GPU at 7B shape; % HBM / fp8 tensor roofline"
 L2_BYTES = 126 * 2 ** 20
-# DRAM bytes (read + write) of one in_proj GEMM launch per token, from an ncu
-# capture of the T = 16384 case (dram__bytes_read.sum + dram__bytes_write.sum =
-# 269350912 + 377080576 B), scaled by T
-IN_PROJ_DRAM_BYTES_PER_TOKEN = (269350912 + 377080576) / 16384
+# DRAM bytes (read + write) of one in_proj GEMM launch (the SM-pair kernel) per
+# token, from an ncu capture of the T = 16384 case (dram__bytes_read.sum +
+# dram__bytes_write.sum = 446.2 + 376.3 MB), scaled by T
+IN_PROJ_DRAM_BYTES_PER_TOKEN = (446246400 + 376256768) / 16384
 
 
 # ---------------------------------------------------------------- synthetic model
