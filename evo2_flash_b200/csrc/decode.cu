@@ -554,140 +554,138 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   store_bf16x4(out, g);
 }
 
-// LI q = 1 decode.  A block covers 64 channels of IIR_R requests in two
-// phases.  Gate phase: one thread per (request, 4 channels) runs the short
-// filter + gate (4-wide vector path, S0 window written) into shared memory.
-// State phase: four threads per channel, each owning four of its 16 modes, so
-// that a warp streams 8 channels x 64 bytes of state with one coalesced
-// 16-byte access per thread; poles, residues and exp(log_pole) are loaded once
-// for all requests and every state load is issued before the gate phase.  The
-// readout keeps the halving tree of modal_readout16 exactly: modes s and s+8
-// meet across threads t and t+2, s and s+4 across t and t+1, the rest inside
-// thread 0.
-constexpr int IIR_R = 8;
-constexpr int IIR_CH = 64;
+// LI q = 1 decode, one lane per channel for LQ_R requests: a block holds 128
+// consecutive channels and needs no barrier, so its warps run independently.
+// A lane computes its channel's exp(log-pole)s and loads its residues, short
+// taps and D once for all its requests; it then walks the requests with the
+// next request's state row (16-byte loads), z triple and window columns in
+// flight while the current one is computed: the K=3 filter of the triple
+// (short_tap, the arithmetic of decode_kernel), the 16 modes advanced in packed
+// f32x2 arithmetic (same roundings), the row and the shifted window written
+// back, modal_readout16's halving tree.
+constexpr int LQ_THREADS = 128;
+constexpr int LQ_R = 4;
 
-// modal_readout16 over a channel's 16 modes held by four consecutive lanes
-// (lane t of the quad owns modes 4t .. 4t+3): the same halving tree, modes s
-// and s + 8 meeting across lanes t and t^2, s and s + 4 across t and t^1, the
-// rest inside lane 0 of the quad, which alone returns the readout.  Called by
-// all 32 lanes of the warp.
-__device__ __forceinline__ float quad_readout(const float (&s4)[4], const float (&res)[4]) {
-  const unsigned full = 0xffffffffu;
-  float q[4], o[4];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) q[m] = mul_rn(s4[m], res[m]);
-#pragma unroll
-  for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 2);
-#pragma unroll
-  for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 8] (t < 2)
-#pragma unroll
-  for (int m = 0; m < 4; ++m) o[m] = __shfl_xor_sync(full, q[m], 1);
-#pragma unroll
-  for (int m = 0; m < 4; ++m) q[m] = add_rn(q[m], o[m]);  // p[s] += p[s + 4] (t == 0)
-  q[0] = add_rn(q[0], q[2]);
-  q[1] = add_rn(q[1], q[3]);
-  return add_rn(q[0], q[1]);
-}
-constexpr int IIR_THREADS = 256;
-static_assert(IIR_R * IIR_CH / 4 <= IIR_THREADS, "one gate item per thread");
+struct LqIn {
+  float4 sv[4];                // the 16-mode row
+  bf16 z[3], c0[3], c1[3];     // z triple, window columns 0 and 1
+};
 
-__global__ void __launch_bounds__(IIR_THREADS, 3)
-decode_iir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
-  __shared__ long long route[4][IIR_R];  // cin, cout, src, dst per request
-  __shared__ float u_s[IIR_R][IIR_CH], x2_s[IIR_R][IIR_CH];
+__global__ void __launch_bounds__(LQ_THREADS)
+decode_iir_q1_lane_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   pdl_entry();
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int t = lane & 3;    // modes 4t .. 4t+3
-  const int cl = warp * 8 + (lane >> 2);  // channel within the block
-  const int hb = blockIdx.x * IIR_CH;
-  const int h = hb + cl;     // H % 64 == 0: always a valid channel
-  const int r0 = blockIdx.y * IIR_R;
-  if (threadIdx.x < 4 * IIR_R) {
-    const int i = threadIdx.x % IIR_R, f = threadIdx.x / IIR_R, r = r0 + i;
-    long long v = -1;
-    if (r < A.num_reqs) {
-      if (f == 0) v = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
-      else if (f == 1) v = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
-      else if (f == 2) v = __ldg(A.in_slots + (long long)r * A.in_stride0);
-      else v = __ldg(A.out_slots + (long long)r * A.out_stride0);
+  const int r0 = blockIdx.x * LQ_R;
+  const int h = blockIdx.y * LQ_THREADS + threadIdx.x;
+  if (h >= P.H) return;
+  const int nr = min(LQ_R, A.num_reqs - r0);
+  // routing of the lane's requests, all loads at once
+  long long cin[LQ_R], cout[LQ_R], src[LQ_R], dst[LQ_R];
+#pragma unroll
+  for (int i = 0; i < LQ_R; ++i) {
+    cin[i] = cout[i] = src[i] = dst[i] = -1;
+    if (i < nr) {
+      const int r = r0 + i;
+      cin[i] = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
+      cout[i] = __ldg(A.conv_out_block + (long long)r * A.conv_out_stride);
+      src[i] = __ldg(A.in_slots + (long long)r * A.in_stride0);
+      dst[i] = __ldg(A.out_slots + (long long)r * A.out_stride0);
     }
-    route[f][i] = v;
   }
   float* st = static_cast<float*>(A.inner_state.data);
-  const float4 lp4 = __ldg(reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h) + t);
-  const float4 rs4 = __ldg(reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h) + t);
+  const long long D = A.inner_state.dim_stride;
+  const bf16* s0 = static_cast<const bf16*>(A.conv_state.data);
+  auto zero_row = [&](int i) {
+    return (A.zero_null_rows && cin[i] == A.null_block) || !block_ok(cin[i], A.conv_state);
+  };
+  auto load = [&](int i, LqIn& in) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) in.sv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (zero_row(i)) return;
+    if (block_ok(src[i], A.inner_state)) {
+      const float4* sp = reinterpret_cast<const float4*>(st + src[i] * A.inner_state.block_stride + h * D);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) in.sv[k] = sp[k];
+    }
+    const bf16* zr = static_cast<const bf16*>(A.z) + (long long)(r0 + i) * A.ldz + 3 * h;
+    const bf16* w0p = s0 + cin[i] * A.conv_state.block_stride + 3 * h;
+    const bf16* w1p = w0p + A.conv_state.col_stride;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      in.z[j] = zr[j];
+      in.c0[j] = w0p[j];
+      in.c1[j] = w1p[j];
+    }
+  };
+  LqIn cur;
+  load(0, cur);
+  // per-channel parameters, once for all requests
+  float w[9];
+  const bf16* swp = static_cast<const bf16*>(P.short_w) + 9 * h;
+#pragma unroll
+  for (int j = 0; j < 9; ++j) w[j] = __bfloat162float(__ldg(swp + j));
+  const float4* lp4 = reinterpret_cast<const float4*>(P.log_poles + (long long)h * P.lp_stride_h);
+  const float4* rs4 = reinterpret_cast<const float4*>(P.residues + (long long)h * P.res_stride_h);
+  float2 pl2[8], rs2[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 a = __ldg(lp4 + k), b = __ldg(rs4 + k);
+    pl2[2 * k] = make_float2(expf(a.x), expf(a.y));
+    pl2[2 * k + 1] = make_float2(expf(a.z), expf(a.w));
+    rs2[2 * k] = make_float2(b.x, b.y);
+    rs2[2 * k + 1] = make_float2(b.z, b.w);
+  }
   const bf16* Dg = static_cast<const bf16*>(P.D);
   const float dval = Dg ? ldbf(Dg + h) : 0.0f;
-  __syncthreads();
 
-  // Request flags (uniform across the block) and every state load.
-  unsigned live = 0, zero = 0, dok = 0;
-  float4 sv[IIR_R];
 #pragma unroll
-  for (int i = 0; i < IIR_R; ++i) {
-    const long long cin = route[0][i], src = route[2][i], dst = route[3][i];
-    const bool lv = r0 + i < A.num_reqs;
-    const bool zr = lv && ((A.zero_null_rows && cin == A.null_block) || !block_ok(cin, A.conv_state));
-    const bool src_ok = block_ok(src, A.inner_state);
-    const bool dk = lv && !zr && block_ok(dst, A.inner_state) &&
-                    !(A.skip_null_writes && dst == A.null_block);
-    if (threadIdx.x == 0 && lv && (!block_ok(cin, A.conv_state) || (!zr && !src_ok)))
-      flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
-    live |= unsigned(lv) << i;
-    zero |= unsigned(zr) << i;
-    dok |= unsigned(dk) << i;
-    sv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (lv && !zr && src_ok)
-      sv[i] = *reinterpret_cast<const float4*>(st + src * A.inner_state.block_stride +
-                                               (long long)h * A.inner_state.dim_stride + 4 * t);
-  }
-  // Gate phase: item = (request i, channels 4 c4 .. 4 c4 + 3 of the block).
-  if (threadIdx.x < IIR_R * IIR_CH / 4) {
-    const int i = threadIdx.x / (IIR_CH / 4), c4 = threadIdx.x % (IIR_CH / 4);
-    if ((live >> i) & 1u) {
-      float gx2[4] = {0.f, 0.f, 0.f, 0.f}, gu[4] = {0.f, 0.f, 0.f, 0.f};
-      if (!((zero >> i) & 1u)) {
-        const long long cin = route[0][i], cout = route[1][i];
-        GateIn<4> gin;
-        gate_load<4>(P, A, r0 + i, hb + 4 * c4, cin, gin);
-        const bool write_conv =
-            block_ok(cout, A.conv_state) && !(A.skip_null_writes && cout == A.null_block);
-        gate_finish<4>(A, hb + 4 * c4, cout, write_conv, gin, gx2, gu);
+  for (int i = 0; i < LQ_R; ++i) {
+    if (i >= nr) break;
+    LqIn nxt;
+    if (i + 1 < nr) load(i + 1, nxt);
+    bf16* out = static_cast<bf16*>(A.out) + (long long)(r0 + i) * A.ldo + h;
+    if (zero_row(i)) {
+      if (!block_ok(cin[i], A.conv_state) && threadIdx.x == 0)
+        flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+      *out = __float2bfloat16_rn(0.0f);
+    } else {
+      if (!block_ok(src[i], A.inner_state) && threadIdx.x == 0)
+        flag_error(A.error_flags, HYENA_FLAG_BLOCK_RANGE);
+      float o[3];
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        o[j] = short_tap(__bfloat162float(cur.c0[j]), __bfloat162float(cur.c1[j]),
+                         __bfloat162float(cur.z[j]), w[3 * j], w[3 * j + 1], w[3 * j + 2]);
+      const float x2 = o[0];
+      const float u = bf16r(o[1] * o[2]);
+      if (block_ok(cout[i], A.conv_state) && !(A.skip_null_writes && cout[i] == A.null_block)) {
+        bf16* d0 = static_cast<bf16*>(A.conv_state.data) + cout[i] * A.conv_state.block_stride + 3 * h;
+        bf16* d1 = d0 + A.conv_state.col_stride;
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {  // window <- [old column 1, this row]
+          d0[j] = cur.c1[j];
+          d1[j] = cur.z[j];
+        }
       }
+      float2 s2[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        u_s[i][4 * c4 + e] = gu[e];
-        x2_s[i][4 * c4 + e] = gx2[e];
+      for (int k = 0; k < 4; ++k) {
+        s2[2 * k] = make_float2(cur.sv[k].x, cur.sv[k].y);
+        s2[2 * k + 1] = make_float2(cur.sv[k].z, cur.sv[k].w);
       }
-    }
-  }
-  __syncthreads();
-  const float pole[4] = {expf(lp4.x), expf(lp4.y), expf(lp4.z), expf(lp4.w)};
-  const float res[4] = {rs4.x, rs4.y, rs4.z, rs4.w};
-  bf16* outp = static_cast<bf16*>(A.out);
+      const float2 u2 = make_float2(u, u);
 #pragma unroll
-  for (int i = 0; i < IIR_R; ++i) {
-    if (!((live >> i) & 1u)) continue;  // uniform
-    const long long orow = (long long)(r0 + i) * A.ldo;
-    if ((zero >> i) & 1u) {
-      if (t == 0) outp[orow + h] = __float2bfloat16_rn(0.0f);
-      continue;
-    }
-    const float u = u_s[i][cl], x2 = x2_s[i][cl];
-    float s4[4] = {sv[i].x, sv[i].y, sv[i].z, sv[i].w};
+      for (int k = 0; k < 8; ++k) s2[k] = fadd2(fmul2(s2[k], pl2[k]), u2);  // s p + u, no FMA
+      if (block_ok(dst[i], A.inner_state) && !(A.skip_null_writes && dst[i] == A.null_block)) {
+        float4* dp = reinterpret_cast<float4*>(st + dst[i] * A.inner_state.block_stride + h * D);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) s4[m] = add_rn(mul_rn(s4[m], pole[m]), u);
-    if ((dok >> i) & 1u)
-      *reinterpret_cast<float4*>(st + route[3][i] * A.inner_state.block_stride +
-                                 (long long)h * A.inner_state.dim_stride + 4 * t) =
-          make_float4(s4[0], s4[1], s4[2], s4[3]);
-    const float yr = quad_readout(s4, res);
-    if (t == 0) {
-      float y = bf16r(yr);
+        for (int k = 0; k < 4; ++k)
+          dp[k] = make_float4(s2[2 * k].x, s2[2 * k].y, s2[2 * k + 1].x, s2[2 * k + 1].y);
+      }
+      float y = bf16r(modal_readout16_x2(s2, rs2));
       if (Dg) y = bf16r(y + bf16r(dval * u));
-      outp[orow + h] = __float2bfloat16_rn(bf16r(x2 * y));
+      *out = __float2bfloat16_rn(bf16r(x2 * y));
     }
+    if (i + 1 < nr) cur = nxt;
   }
 }
 
@@ -1250,9 +1248,9 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& args, cu
     return fail(HYENA_ERR_UNSUPPORTED, "conv window wider than 8 columns");
   if (fast_path_ok(P, A)) {
     if (P.kind == HYENA_KIND_IIR && P.K == 16) {
-      dim3 g(P.H / 64, (A.num_reqs + IIR_R - 1) / IIR_R);
-      launch_kernel(decode_iir_q1_kernel, dim3(g), dim3(IIR_THREADS), 0, st, 0u, P, A);
-      return check_launch("decode_iir_q1_kernel");
+      dim3 g((A.num_reqs + LQ_R - 1) / LQ_R, (P.H + LQ_THREADS - 1) / LQ_THREADS);
+      launch_kernel(decode_iir_q1_lane_kernel, dim3(g), dim3(LQ_THREADS), 0, st, 0u, P, A);
+      return check_launch("decode_iir_q1_lane_kernel");
     }
     dim3 g(A.num_reqs, (P.H / 4 + FAST_THREADS - 1) / FAST_THREADS);
     if (P.kind == HYENA_KIND_FIR && P.K == 128) {
