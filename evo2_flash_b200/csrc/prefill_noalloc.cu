@@ -5,9 +5,9 @@
 // range table and the carried modal states of the chunked scan.  Some callers
 // have no way to provide one: a host program in another language that reaches
 // this library only through the C ABI and has no CUDA allocator of its own, or
-// an engine that launches from inside CUDA-graph stream capture, where
-// cudaMalloc is not permitted (and elsewhere it synchronises the device, which a
-// per-step call on the serving path must not do).  This entry point takes the
+// a serving loop that may not call cudaMalloc once it runs, because cudaMalloc
+// can synchronise the device and its memory budget was fixed at start-up.
+// This entry point takes the
 // same arguments minus the workspace and uses a fixed scratch array that lives
 // in this library's device memory instead.
 //

@@ -1,9 +1,9 @@
 """hyena_prefill_noalloc: prefill for callers that cannot allocate device memory.
 
 Some hosts reach this library only through its C ABI and have no CUDA allocator
-to hand it a workspace (a Go, Java or Rust program over cgo/JNI/FFI), and an
-engine that launches while a CUDA graph is being captured may not call
-cudaMalloc at all.  This entry point keeps the LI prefill's scratch in a fixed
+to hand it a workspace (a Go, Java or Rust program over cgo/JNI/FFI), and a
+serving loop may not call cudaMalloc once it runs, since cudaMalloc can
+synchronise the device.  This entry point keeps the LI prefill's scratch in a fixed
 device array inside the library instead.  The test calls it through the C ABI
 twice in a row (a fresh prefill, then a continuation that reads the state the
 first call wrote) and compares output and paged state with hyena_prefill run
