@@ -222,7 +222,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             bf16* __restrict__ out, int64_t ldo, int M, int N, int K,
             const float* __restrict__ sa, const float* __restrict__ sb,
             const bf16* __restrict__ bias) {
-  pdl_trigger();
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = Cfg<BN>::TMEM_COLS;
@@ -270,6 +269,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     for (int kb = 0; kb < kblocks && kb < STAGES; ++kb) tma_prefetch_l2(&tmB, kb * KE, n0);
   }
   pdl_wait();
+  pdl_trigger();  // after the wait: see common.cuh
 
   if (warp == 0) {
     if (lane == 0) {
@@ -479,7 +479,6 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, bf16* __restrict__ out, int64_t ldo,
                     int M, int N, int K, const float* __restrict__ sa,
                     const float* __restrict__ sb, const bf16* __restrict__ bias) {
-  pdl_trigger();
   constexpr int STAGES = Cfg<BN>::STAGES;
   constexpr int STAGE_BYTES = Cfg<BN>::STAGE_BYTES;
   constexpr uint32_t TMEM_COLS = pow2_cols<BN>();
@@ -538,6 +537,7 @@ gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmA,
     for (int kb = kb0; kb < kb1 && kb < kb0 + STAGES; ++kb) tma_prefetch_l2(&tmB, kb * KE, n0);
   }
   pdl_wait();
+  pdl_trigger();  // after the wait: see common.cuh
 
   if (warp == 0) {
     if (lane == 0) {
