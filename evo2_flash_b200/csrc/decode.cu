@@ -336,8 +336,12 @@ decode_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 // Ordinary decode (one token per request, accepted = 1, a 2-column short window
 // with unit channel stride): a thread owns 4 consecutive channels (FIR) or one
 // channel's 16 modes (IIR) and streams its state with 16-byte accesses, 16 taps in
-// flight.  Same arithmetic, order and rounding as decode_kernel.
+// flight.  Same arithmetic, order and rounding as decode_kernel.  The verify
+// kernels use blocks of FAST_THREADS, the one-token FIR kernel blocks of
+// Q1_THREADS (64: 1.1 us faster per decode step of the 7B triple at 128
+// requests than 128; 64 made the verify step 0.507 -> 0.530 ms).
 constexpr int FAST_THREADS = 128;
+constexpr int Q1_THREADS = 64;
 
 __device__ __forceinline__ void load_bf16x4(const bf16* p, float (&v)[4]) {
   const uint2 r = *reinterpret_cast<const uint2*>(p);
@@ -471,13 +475,13 @@ __device__ __forceinline__ void gate_finish(const hyena_decode_args& A, int h, l
 }
 
 template <int K>
-__global__ void __launch_bounds__(FAST_THREADS)
+__global__ void __launch_bounds__(Q1_THREADS)
 decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   pdl_entry();
   constexpr int HIST = K - 1;
   constexpr int U = 8;  // taps in flight
   const int r = blockIdx.x;
-  const int h = 4 * (blockIdx.y * FAST_THREADS + threadIdx.x);
+  const int h = 4 * (blockIdx.y * Q1_THREADS + threadIdx.x);
   if (h >= P.H) return;
   // Routing first, all four loads in flight at once.
   const long long cin = __ldg(A.conv_in_block + (long long)r * A.conv_in_stride);
@@ -554,8 +558,10 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
   store_bf16x4(out, g);
 }
 
-// LI q = 1 decode, one lane per channel for LQ_R requests: a block holds 128
-// consecutive channels and needs no barrier, so its warps run independently.
+// LI q = 1 decode, one lane per channel for LQ_R requests: a block holds
+// LQ_THREADS consecutive channels and needs no barrier, so its warps run
+// independently (64-lane blocks: 0.6 us faster per decode step than 128 or
+// 256; two requests per lane instead of four: 1.7 us slower).
 // A lane computes its channel's exp(log-pole)s and loads its residues, short
 // taps and D once for all its requests; it then walks the requests with the
 // next request's state row (16-byte loads), z triple and window columns in
@@ -563,7 +569,7 @@ decode_fir_q1_kernel(const hyena_layer_params P, const hyena_decode_args A) {
 // (short_tap, the arithmetic of decode_kernel), the 16 modes advanced in packed
 // f32x2 arithmetic (same roundings), the row and the shifted window written
 // back, modal_readout16's halving tree.
-constexpr int LQ_THREADS = 128;
+constexpr int LQ_THREADS = 64;
 constexpr int LQ_R = 4;
 
 struct LqIn {
@@ -1252,13 +1258,13 @@ int decode_launch(const hyena_layer_params& P, const hyena_decode_args& args, cu
       launch_kernel(decode_iir_q1_lane_kernel, dim3(g), dim3(LQ_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_iir_q1_lane_kernel");
     }
-    dim3 g(A.num_reqs, (P.H / 4 + FAST_THREADS - 1) / FAST_THREADS);
+    dim3 g(A.num_reqs, (P.H / 4 + Q1_THREADS - 1) / Q1_THREADS);
     if (P.kind == HYENA_KIND_FIR && P.K == 128) {
-      launch_kernel(decode_fir_q1_kernel<128>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
+      launch_kernel(decode_fir_q1_kernel<128>, dim3(g), dim3(Q1_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_fir_q1_kernel<128>");
     }
     if (P.kind == HYENA_KIND_FIR && P.K == 7) {
-      launch_kernel(decode_fir_q1_kernel<7>, dim3(g), dim3(FAST_THREADS), 0, st, 0u, P, A);
+      launch_kernel(decode_fir_q1_kernel<7>, dim3(g), dim3(Q1_THREADS), 0, st, 0u, P, A);
       return check_launch("decode_fir_q1_kernel<7>");
     }
   }
