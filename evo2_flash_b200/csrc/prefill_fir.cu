@@ -610,9 +610,13 @@ static int launch_fir(const hyena_layer_params& P, const hyena_prefill_args& A, 
   if (!smem_attr<fir_prefill_kernel<K>>((int)smem))
     return fail(HYENA_ERR_CUDA, "cudaFuncSetAttribute(fir_prefill) failed");
   // Rows per CTA: a multiple of the tile, long enough that the (K-1)-row halo is
-  // a small fraction, short enough to fill the 148 SMs several times over.
+  // a small fraction, short enough to fill the 148 SMs several times over.  A
+  // CTA whose rows start inside a segment recomputes the halo's u from z with
+  // scalar loads: at the config-2 shape (8 x 8192 rows, H = 4096) 8192-row
+  // CTAs, which start at segment starts, took HCM 0.884 -> 0.800 ms and HCS
+  // 0.610 -> 0.588 ms against 4096 rows (2048 rows: 1.037 / 0.656 ms).
   const int groups = P.H / FIR_CG;
-  int rows = 4096;
+  int rows = 8192;
   const long long want_ctas = 148LL * 8;
   while (rows > FIR_BT && (long long)((A.T + rows - 1) / rows) * groups < want_ctas) rows /= 2;
   while ((A.T + rows - 1) / rows > 65535) rows *= 2;
