@@ -318,20 +318,100 @@ class StripedHyena2(nn.Module):
                 layer.mixer.allocate_state(num_blocks, self.device)
 
     # ---- forward ------------------------------------------------------------------
-    def forward(self, input_ids, positions, meta, segments):
-        """Hidden states after the final norm for one packed prefill step.
-        `meta`: mixer metadata (prefill-only); `segments`: (row_start, row_end,
-        seq_id, first_position) per sequence chunk in the step."""
+    def forward(self, input_ids, positions, meta, segments, block_outputs=None):
+        """Hidden states after the final norm for one packed step.
+        `meta`: mixer metadata (prefill rows, or one-token decode rows);
+        `segments`: (row_start, row_end, seq_id, first_position) per sequence
+        chunk in the step.  `block_outputs`: a dict whose integer keys name
+        blocks; each gets that block's output residual stream (m + x + mlp,
+        the reference's block output, model.py:189-198) as a new tensor."""
         x = self.embed[input_ids]
         add = None
         with set_forward_metadata(meta):
-            for layer in self.layers:
+            for i, layer in enumerate(self.layers):
                 add, x = layer(x, positions, segments, add, input_ids)
+                if block_outputs is not None and i in block_outputs:
+                    block_outputs[i] = x + add
         return self.norm.add_norm_(add, x)
 
     def logprobs(self, h, targets):
         logits = F.linear(h, self.embed).float()
         return torch.log_softmax(logits, -1).gather(1, targets[:, None]).squeeze(1)
+
+    @torch.no_grad()
+    def prefill_steps(self, seqs, max_tokens_per_step=None, block_outputs=None, keep_cache=False):
+        """Teacher-forced prefill of `seqs` (1-D int token tensors) packed in
+        order into steps of at most `max_tokens_per_step` tokens (default: all
+        in one step); a sequence that does not fit finishes in later steps from
+        its cached state (has_initial_state).  Sequence j owns state block j + 1
+        (block 0 is the null block) and attention cache entry j; with
+        keep_cache the attention entries stay after the last step, so that
+        decode_step can continue the sequences (else each is dropped once its
+        sequence is done).  Yields (h, segments) per step: h (rows, H) after
+        the final norm.
+        `block_outputs` (a set of block indices) adds a third item, the dict of
+        those blocks' outputs for the step's rows."""
+        dev = self.device
+        lens = [int(s.numel()) for s in seqs]
+        budget = max_tokens_per_step or max(1, sum(lens))
+        self.allocate_state(len(seqs) + 1)
+        for layer in self.layers:
+            if layer.kind == "attn":
+                layer.mixer.kv.clear()
+        done = [0] * len(seqs)
+        nxt = 0
+        while nxt < len(seqs) and lens[nxt] == 0:
+            nxt += 1
+        while nxt < len(seqs):
+            rows, segs, used = [], [], 0
+            j = nxt
+            while j < len(seqs) and used < budget:
+                take = min(lens[j] - done[j], budget - used)
+                if take > 0:
+                    segs.append((used, used + take, j, done[j]))
+                    rows.append(seqs[j][done[j]:done[j] + take])
+                    used += take
+                if done[j] + take < lens[j]:
+                    break
+                j += 1
+            ids = torch.cat(rows).to(dev)
+            positions = torch.cat([torch.arange(p0, p0 + (b - a)) for a, b, _, p0 in segs]).to(dev)
+            meta = _prefill_meta(segs, dev)
+            taps = None if block_outputs is None else dict.fromkeys(block_outputs)
+            h = self(ids, positions, meta, segs, taps)
+            yield (h, segs) if taps is None else (h, segs, taps)
+            for a, b, sid, p0 in segs:
+                done[sid] = p0 + (b - a)
+                if done[sid] == lens[sid] and not keep_cache:
+                    for layer in self.layers:
+                        if layer.kind == "attn":
+                            layer.mixer.release(sid)
+            while nxt < len(seqs) and done[nxt] == lens[nxt]:
+                nxt += 1
+
+    @torch.no_grad()
+    def token_logprobs(self, seqs, max_tokens_per_step=None):
+        """log p(x_t | x_<t) for t = 1 .. L-1 of each sequence (fp32 log-softmax,
+        float64 values on the CPU), by teacher-forced prefill_steps."""
+        lens = [int(s.numel()) for s in seqs]
+        out = [torch.empty(max(0, n - 1), dtype=torch.float64) for n in lens]
+        for h, segs in self.prefill_steps(seqs, max_tokens_per_step):
+            tgt_rows, tgt, dst = [], [], []
+            for a, b, sid, p0 in segs:
+                last = min(b - a, lens[sid] - 1 - p0)  # rows with a next token
+                if last > 0:
+                    tgt_rows.append(torch.arange(a, a + last))
+                    tgt.append(seqs[sid][p0 + 1:p0 + 1 + last])
+                    dst.append((sid, p0, last))
+            if tgt_rows:
+                r = torch.cat(tgt_rows).to(self.device)
+                lp = self.logprobs(h[r], torch.cat(tgt).to(self.device)).double().cpu()
+                off = 0
+                for sid, p0, last in dst:
+                    out[sid][p0:p0 + last] = lp[off:off + last]
+                    off += last
+        self.release_all()
+        return out
 
     @torch.no_grad()
     def score(self, seqs, max_tokens_per_step=None):
@@ -390,6 +470,25 @@ class StripedHyena2(nn.Module):
                 nxt += 1
         return [-s / c if c else math.nan for s, c in zip(sums, cnt)]
 
+    @torch.no_grad()
+    def decode_step(self, token_ids, positions, seq_ids):
+        """One token for each of the given sequences, continuing their cached
+        state (Hyena: one-token decode rows on state block seq_id + 1; attention:
+        the sequence's key/value cache): (B, H) hidden states after the final
+        norm.  token_ids, positions: (B,) ints; seq_ids: B distinct ints."""
+        dev = self.device
+        ids = torch.as_tensor(token_ids, dtype=torch.long).to(dev)
+        pos = torch.as_tensor(positions, dtype=torch.long)
+        segs = [(i, i + 1, int(sid), int(p)) for i, (sid, p) in enumerate(zip(seq_ids, pos.tolist()))]
+        meta = _decode_meta([int(sid) + 1 for sid in seq_ids], dev)
+        return self(ids, pos.to(dev), meta, segs)
+
+    def release_all(self):
+        """Drops every sequence's attention key/value cache."""
+        for layer in self.layers:
+            if layer.kind == "attn":
+                layer.mixer.kv.clear()
+
 
 def _prefill_meta(segs, device):
     """Prefill-only mixer metadata for one step; sequence j owns state block j+1."""
@@ -408,3 +507,16 @@ def _prefill_meta(segs, device):
         query_start_loc_d=None, num_accepted_tokens=None,
         seq_lens=torch.tensor([p0 + (b - a) for a, b, _, p0 in segs], dtype=torch.int32,
                               device=device))
+
+
+def _decode_meta(blocks, device):
+    """One-token decode metadata for the mixers: request i on state block blocks[i]."""
+    n = len(blocks)
+    return SimpleNamespace(
+        num_decodes=n, num_decode_tokens=n, num_prefills=0, num_prefill_tokens=0,
+        query_start_loc_p=torch.zeros(1, dtype=torch.int32, device=device),
+        has_initial_states_p=torch.zeros(0, dtype=torch.bool, device=device),
+        state_indices_tensor_p=torch.zeros(0, dtype=torch.int32, device=device),
+        state_indices_tensor_d=torch.tensor(blocks, dtype=torch.int32, device=device),
+        query_start_loc_d=None, num_accepted_tokens=None,
+        seq_lens=torch.zeros(n, dtype=torch.int32, device=device))
