@@ -958,6 +958,15 @@ def release_reducers():
     torch.cuda.synchronize()
 
 
+def config2(world, batch):
+    """The `config` of the default line (config 2), shared by both arms."""
+    return {"workload": "config2: HCS+HCM+HCL mixer triple prefill, 7B shape",
+            "model": "StripedHyena2-7B mixer triple (random init)", "hidden": H,
+            "global_batch": batch * world, "seq_len": PREFILL_L,
+            "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (x 512 MiB, z 1.5 GiB per layer)"}
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -1005,10 +1014,10 @@ def main():
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config2: HCS+HCM+HCL triple prefill, H=4096 (sample)",
-                       "tokens_per_step": args.cpu_tokens},
+            "config": config2(args.gpus, args.batch),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": f"1 x {args.cpu_tokens} ACGT tokens through the triple"},
+                             "sample": f"1 x {args.cpu_tokens} ACGT tokens through the triple "
+                                       "per step (a bounded sample of the workload above)"},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }
@@ -1156,10 +1165,7 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3/bf16",
         "data": "synthetic (seeded ACGT, random-init weights)",
-        "config": {"workload": "config2: HCS+HCM+HCL mixer triple prefill, 7B shape",
-                   "model": "StripedHyena2-7B mixer triple (random init)", "hidden": H,
-                   "global_batch": args.batch * world, "seq_len": PREFILL_L,
-                   "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (x 512 MiB, z 1.5 GiB per layer)"},
+        "config": config2(world, args.batch),
         "roofline": {"bound": "tensor", "kernel": "hyena_gemm_e4m3 (in_proj, tcgen05)",
                      "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": achieved / fp8_peak,
