@@ -209,3 +209,24 @@ def test_sample_token_filters():
     assert draws == {1, 2}
     draws = {sample_token(logits, 1.0, 0, 0.5, g) for _ in range(50)}
     assert draws == {1}
+
+
+def test_chunked_prompts_generate_and_forward_like_one_step(evo):
+    """Prompts longer than the step budget are prefilled over several steps
+    (resumed from the paged state) before decoding; forward over chunked steps
+    returns every position's logits."""
+    prompts = [_dna(70, 14), _dna(45, 15)]
+    one = evo.generate(prompts, n_tokens=6, top_k=1, verbose=0)
+    ids = torch.tensor([evo.tokenizer.tokenize(_dna(60, 16))])
+    lg_one, _ = evo.forward(ids)
+    evo.max_tokens_per_step = 24
+    try:
+        chunked = evo.generate(prompts, n_tokens=6, top_k=1, verbose=0)
+        lg_chunked, _ = evo.forward(ids)
+    finally:
+        evo.max_tokens_per_step = None
+    assert [len(t) for t in chunked.token_ids] == [6, 6]
+    assert chunked.logprobs_mean == pytest.approx(one.logprobs_mean, abs=5e-3)
+    lp1 = torch.log_softmax(lg_one.float(), -1)
+    lp2 = torch.log_softmax(lg_chunked.float(), -1)
+    assert (lp1 - lp2).abs().max() < 5e-2
