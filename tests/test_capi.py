@@ -4,6 +4,8 @@ rejects invalid arguments on the host before touching the device."""
 
 import ctypes as C
 import re
+import shutil
+import subprocess
 from pathlib import Path
 
 import pytest
@@ -89,3 +91,45 @@ def test_gemms_need_no_workspace(lib):
     for m in (0, 1, 128, 65536):
         assert lib.hyena_gemm_workspace_size(m, 12288, 4096, 1) == 0
         assert lib.hyena_gemm_workspace_size(m, 4096, 4096, 0) == 0
+
+
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "hyena_b200.h"
+int main(void) {
+  if (hyena_abi_version() != HYENA_ABI_VERSION) return 2;
+  hyena_layer_params p;
+  memset(&p, 0, sizeof p);
+  p.kind = HYENA_KIND_IIR; p.H = 4096; p.K = 16;
+  size_t ws = hyena_prefill_workspace_size(&p, 65536, 8);
+  hyena_prefill_args a;
+  memset(&a, 0, sizeof a);
+  p.kind = HYENA_KIND_FIR; p.H = 100; p.K = 128;
+  int rc = hyena_prefill(&p, &a, NULL, 0, NULL);
+  printf("%zu %d %s\n", ws, rc, hyena_last_error());
+  return 0;
+}
+"""
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_c_host_program_builds_and_calls_the_abi(lib, tmp_path):
+    """A plain C host (no torch, no Python) compiles against the header with
+    warnings as errors, links the library and gets host-side answers from it:
+    the workspace query and an argument rejected before any device work."""
+    from evo2_flash_b200._build import LIB_DIR
+
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                    str(src), f"-L{LIB_DIR}", "-lhyena_b200", f"-Wl,-rpath,{LIB_DIR}",
+                    "-o", str(exe)], check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split(" ", 2)
+    from evo2_flash_b200._lib import LayerParams
+
+    lp = LayerParams()
+    lp.kind, lp.H, lp.K = 1, 4096, 16
+    assert int(out[0]) == lib.hyena_prefill_workspace_size(C.byref(lp), 65536, 8)
+    assert int(out[1]) == 1 and "multiple of 64" in out[2]
