@@ -220,28 +220,72 @@ class Evo2:
         return scores
 
     # ---- forward / embeddings -----------------------------------------------
-    def _block_index(self, name: str):
-        """A layer name -> block index (int), 'norm' or 'unembed'.  Names are the
-        reference's vortex names for the residual stream: 'blocks.N' (after
-        block N), 'norm' (after the final norm), 'unembed' (the logits)."""
-        if name in ("norm", "unembed"):
-            return name
-        parts = name.split(".")
-        if len(parts) == 2 and parts[0] == "blocks" and parts[1].isdigit():
-            i = int(parts[1])
-            if i < len(self.model.layers):
-                return i
-            raise ValueError(f"layer name {name!r}: the model has {len(self.model.layers)} blocks")
-        raise ValueError(f"layer name {name!r} is not supported here; use 'blocks.N', "
-                         "'norm' or 'unembed'")
+    # vortex layer names (evo2_flash/api.py:176-192) -> what the harness captures:
+    # ("embed" | "norm" | "unembed" | "block", block index) or ("module", path,
+    # "out" | "in", kind restriction).  Modules are captured by forward hooks.
+    _NAMES = [
+        (r"embedding_layer", "embed", None, None, None),
+        (r"norm", "norm", None, None, None),
+        (r"unembed", "unembed", None, None, None),
+        (r"blocks\.(\d+)", "block", None, None, None),
+        (r"blocks\.(\d+)\.mlp", "module", "layers.{i}.mlp", "out", None),
+        (r"blocks\.(\d+)\.mlp\.(l1|l2|l3)", "module", "layers.{i}.mlp.{sub}", "out", None),
+        (r"blocks\.(\d+)\.projections", "module", "layers.{i}.mixer.in_proj", "out", "hyena"),
+        (r"blocks\.(\d+)\.filter", "module", "layers.{i}.mixer.out_proj", "in", "hyena"),
+        (r"blocks\.(\d+)\.out_filter_dense", "module", "layers.{i}.mixer.out_proj", "out",
+         "hyena"),
+        (r"blocks\.(\d+)\.inner_mha_cls", "module", "layers.{i}.mixer", "out", "attn"),
+        (r"blocks\.(\d+)\.inner_mha_cls\.out_proj", "module", "layers.{i}.mixer.o_proj", "out",
+         "attn"),
+    ]
+
+    def _resolve(self, name: str):
+        """A vortex layer name -> (what, block index or None, module, "out"/"in")."""
+        import re
+
+        if re.fullmatch(r"blocks\.\d+\.(pre_norm|post_norm)", name):
+            raise ValueError(f"layer name {name!r} is not supported here: this harness "
+                             "applies the block norms inside the residual add (and, for "
+                             "fp8 Hyena layers, inside the in_proj quantisation)")
+        n_blocks = len(self.model.layers)
+        for pat, what, path, io, kind in self._NAMES:
+            m = re.fullmatch(pat, name)
+            if not m:
+                continue
+            i = int(m.group(1)) if m.groups() else None
+            if i is not None:
+                if not 0 <= i < n_blocks:
+                    raise ValueError(f"{name!r}: layer {i} out of range (model has "
+                                     f"{n_blocks} blocks)")
+                is_attn = self.model.layers[i].kind == "attn"
+                if kind == "hyena" and is_attn:
+                    raise ValueError(f"{name!r}: block {i} is an attention block; use "
+                                     f"blocks.{i}.inner_mha_cls instead")
+                if kind == "attn" and not is_attn:
+                    raise ValueError(f"{name!r}: block {i} is a Hyena block; use "
+                                     f"blocks.{i}.filter / blocks.{i}.out_filter_dense instead")
+            if what != "module":
+                return what, i, None, None
+            target = path.format(i=i, sub=m.group(2) if len(m.groups()) > 1 else None)
+            try:
+                mod = self.model.get_submodule(target)
+            except AttributeError:
+                raise ValueError(f"layer name {name!r}: no module {target!r} in this "
+                                 "model") from None
+            return what, i, mod, io
+        raise ValueError(f"unsupported layer name {name!r}; supported: embedding_layer, norm, "
+                         "unembed, blocks.N, blocks.N.mlp[.l1|.l2|.l3], blocks.N.projections, "
+                         "blocks.N.filter, blocks.N.out_filter_dense, blocks.N.inner_mha_cls"
+                         "[.out_proj]")
 
     def forward(self, input_ids, return_embeddings: bool = False, layer_names=None):
         """(logits (B, L, vocab) bf16, embeddings dict or None), each row of
         `input_ids` an independent causal sequence (evo2_flash/api.py:764-808).
-        Embeddings have shape (B, L, H) (logits' shape for 'unembed')."""
+        `layer_names` are vortex names (`blocks.28.mlp.l3`, `blocks.N`, `norm`,
+        ...); each embedding has shape (B, L, D) and the captured tensor's dtype,
+        and 'unembed' is the logits tensor itself."""
         if return_embeddings and layer_names is None:
-            raise ValueError("layer_names must be specified when return_embeddings=True "
-                             "(supported: 'blocks.N', 'norm', 'unembed')")
+            raise ValueError("layer_names must be specified when return_embeddings=True")
         if isinstance(input_ids, torch.Tensor):
             rows = input_ids.detach().long().cpu()
             if rows.dim() == 1:
@@ -265,33 +309,63 @@ class Evo2:
         names = list(layer_names or []) if return_embeddings else []
         if len(set(names)) != len(names):
             raise ValueError(f"duplicate layer names in {names}")
-        targets = {n: self._block_index(n) for n in names}
-        blocks = {t for t in targets.values() if isinstance(t, int)}
+        specs = {n: self._resolve(n) for n in names}
+        blocks = {i for what, i, _, _ in specs.values() if what == "block"}
         B, L = len(id_lists), len(id_lists[0])
         m = self.model
         logits = torch.empty(B, L, V, dtype=torch.bfloat16, device=m.device)
-        emb = {n: torch.empty(B, L, m.cfg.hidden_size, dtype=torch.bfloat16, device=m.device)
-               for n, t in targets.items() if t != "unembed"}
+        emb: dict = {}
+        step_caps: dict = {}
+
+        def hook_for(name, io):
+            def hook(module, args, output):
+                x = args[0] if io == "in" else output
+                if isinstance(x, tuple):
+                    x = x[0]
+                step_caps[name] = x.detach()
+            return hook
+
+        handles = [mod.register_forward_hook(hook_for(n, io))
+                   for n, (what, _, mod, io) in specs.items() if what == "module"]
         seqs = [torch.tensor(x, dtype=torch.long) for x in id_lists]
-        with torch.no_grad():
-            for item in m.prefill_steps(seqs, self.max_tokens_per_step, blocks or None):
-                h, segs = item[0], item[1]
-                taps = item[2] if len(item) > 2 else {}
-                lg = F.linear(h, m.embed)
-                for a, b, sid, p0 in segs:
-                    rows = slice(p0, p0 + (b - a))
-                    logits[sid, rows] = lg[a:b]
-                    for n, t in targets.items():
-                        if t == "norm":
-                            emb[n][sid, rows] = h[a:b]
-                        elif isinstance(t, int):
-                            emb[n][sid, rows] = taps[t][a:b]
+        try:
+            with torch.no_grad():
+                for item in m.prefill_steps(seqs, self.max_tokens_per_step, blocks or None):
+                    h, segs = item[0], item[1]
+                    taps = item[2] if len(item) > 2 else {}
+                    lg = F.linear(h, m.embed)
+                    for n, (what, i, _, _) in specs.items():
+                        if what == "module" and n not in step_caps:
+                            raise RuntimeError(f"layer {n!r} was not captured: its module did "
+                                               "not run in this step")
+                        src = {"norm": h, "block": taps.get(i), "module": step_caps.get(n)}.get(what)
+                        if src is None:
+                            continue
+                        if n not in emb:
+                            emb[n] = torch.empty(B, L, *src.shape[1:], dtype=src.dtype,
+                                                 device=src.device)
+                    for a, b, sid, p0 in segs:
+                        rows = slice(p0, p0 + (b - a))
+                        logits[sid, rows] = lg[a:b]
+                        for n, (what, i, _, _) in specs.items():
+                            if what == "norm":
+                                emb[n][sid, rows] = h[a:b]
+                            elif what == "block":
+                                emb[n][sid, rows] = taps[i][a:b]
+                            elif what == "module":
+                                emb[n][sid, rows] = step_caps[n][a:b]
+                    step_caps.clear()
+        finally:
+            for hd in handles:
+                hd.remove()
         if not return_embeddings:
             return logits, None
-        for n, t in targets.items():
-            if t == "unembed":
+        for n, (what, _, _, _) in specs.items():
+            if what == "unembed":
                 emb[n] = logits
-        return logits, emb
+            elif what == "embed":
+                emb[n] = m.embed[torch.tensor(id_lists, dtype=torch.long, device=m.device)]
+        return logits, {k: emb[k] for k in names}
 
     def __call__(self, input_ids, return_embeddings: bool = False, layer_names=None):
         return self.forward(input_ids, return_embeddings, layer_names)

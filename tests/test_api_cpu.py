@@ -120,7 +120,15 @@ def test_forward_logits_and_embeddings(evo):
     with pytest.raises(ValueError, match="layer_names"):
         evo.forward(ids, return_embeddings=True)
     with pytest.raises(ValueError, match="not supported"):
-        evo.forward(ids, return_embeddings=True, layer_names=["blocks.0.mlp.l3"])
+        evo.forward(ids, return_embeddings=True, layer_names=["blocks.0.pre_norm"])
+    with pytest.raises(ValueError, match="unsupported layer name"):
+        evo.forward(ids, return_embeddings=True, layer_names=["blocks.0.bogus"])
+    with pytest.raises(ValueError, match="attention block"):
+        evo.forward(ids, return_embeddings=True, layer_names=["blocks.3.filter"])
+    with pytest.raises(ValueError, match="Hyena block"):
+        evo.forward(ids, return_embeddings=True, layer_names=["blocks.0.inner_mha_cls"])
+    with pytest.raises(ValueError, match="out of range"):
+        evo.forward(ids, return_embeddings=True, layer_names=["blocks.99"])
     with pytest.raises(ValueError, match="token ids"):
         evo.forward([[0, 600]])
 
@@ -230,3 +238,30 @@ def test_chunked_prompts_generate_and_forward_like_one_step(evo):
     lp1 = torch.log_softmax(lg_one.float(), -1)
     lp2 = torch.log_softmax(lg_chunked.float(), -1)
     assert (lp1 - lp2).abs().max() < 5e-2
+
+
+def test_forward_module_embeddings_by_vortex_name(evo):
+    """Module outputs by the reference's vortex names, captured by forward hooks:
+    the MLP and its l1..l3, the attention mixer and its o_proj, the embedding."""
+    ids = torch.tensor([evo.tokenizer.tokenize(_dna(40, 17))])
+    names = ["blocks.0.mlp", "blocks.0.mlp.l3", "blocks.1.mlp.l1", "blocks.3.inner_mha_cls",
+             "blocks.3.inner_mha_cls.out_proj", "embedding_layer", "blocks.2"]
+    logits, emb = evo(ids, return_embeddings=True, layer_names=names)
+    cfg = evo.model.cfg
+    assert list(emb) == names
+    assert emb["blocks.1.mlp.l1"].shape == (1, 40, cfg.intermediate_size)
+    assert torch.equal(emb["blocks.0.mlp"], emb["blocks.0.mlp.l3"])  # the MLP's output is l3's
+    assert torch.equal(emb["blocks.3.inner_mha_cls"], emb["blocks.3.inner_mha_cls.out_proj"])
+    assert torch.equal(emb["embedding_layer"], evo.model.embed[ids])
+    # the same names over chunked steps give the same rows
+    evo.max_tokens_per_step = 16
+    try:
+        _, emb2 = evo(ids, return_embeddings=True, layer_names=["blocks.0.mlp.l3"])
+    finally:
+        evo.max_tokens_per_step = None
+    from tests.helpers import REL_TOL, max_rel_err
+
+    assert max_rel_err(emb2["blocks.0.mlp.l3"].float(), emb["blocks.0.mlp.l3"].float()) < REL_TOL
+    # Hyena-module names need the B200 mixers' in_proj / out_proj submodules
+    with pytest.raises(ValueError, match="no module"):
+        evo(ids, return_embeddings=True, layer_names=["blocks.0.projections"])

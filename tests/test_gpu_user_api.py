@@ -4,7 +4,8 @@ every Hyena mixer computed by the CPU oracle) within the path's NLL bar; the
 decode steps' hidden states (prompt prefill, then one-token steps through the
 decode kernels) against one teacher-forced prefill within the path's bar, with
 a decode from a zeroed mixer state as the control that must miss it; and
-`generate`'s logprobs_mean against teacher-forced scoring of its own text."""
+`generate`'s logprobs_mean against teacher-forced scoring of its own text;
+embeddings by vortex name, the Hyena projections' included."""
 
 import math
 
@@ -52,7 +53,14 @@ def test_evo2_surface_on_the_b200_mixers():
         lp = gpu.token_logprobs([full])[0][len(pr) - 1:]
         assert abs(float(lp.mean()) - mean) <= NLL_TOL, (float(lp.mean()), mean)
 
-    lg, emb = eg(torch.tensor([eg.tokenizer.tokenize(_dna(64, 50))]), return_embeddings=True,
-                 layer_names=["blocks.2", "norm"])
+    ids = torch.tensor([eg.tokenizer.tokenize(_dna(64, 50))])
+    lg, emb = eg(ids, return_embeddings=True,
+                 layer_names=["blocks.2", "norm", "blocks.1.projections", "blocks.1.filter",
+                              "blocks.1.out_filter_dense"])
     assert lg.shape == (1, 64, 512) and emb["blocks.2"].shape == (1, 64, 256)
+    assert emb["blocks.1.projections"].shape == (1, 64, 768)  # the in_proj triple, 3H
+    assert emb["blocks.1.filter"].shape == emb["blocks.1.out_filter_dense"].shape == (1, 64, 256)
     assert bool(torch.isfinite(lg.float()).all())
+    # hooks on a layer's projections leave its output as it was
+    lg0, _ = eg(ids)
+    assert torch.equal(lg, lg0)
